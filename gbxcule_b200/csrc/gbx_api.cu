@@ -1,0 +1,548 @@
+// gbx_api.cu - the C ABI (include/gbx.h): handle lifetime, device buffers,
+// launches and host transfers. No exception crosses the boundary; every entry
+// point returns a gbx_status and leaves a message in gbx_last_error().
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <new>
+#include <string>
+
+#include "../../include/gbx.h"
+#include "gbx_layout.h"
+
+namespace gbx {
+cudaError_t launch_step(const DevState& st, const int32_t* actions, int frames, int release, int stage,
+                        cudaStream_t stream);
+cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
+                          cudaStream_t stream);
+cudaError_t launch_init(const DevState& st, cudaStream_t s);
+cudaError_t launch_snapshot(const DevState& st, const Snapshot& snap, int env, cudaStream_t s);
+cudaError_t launch_restore(const DevState& st, const Snapshot& snap, const uint8_t* mask, cudaStream_t s);
+cudaError_t launch_to_env_major(const uint8_t* src, uint8_t* dst, int rows, int S, int lo, int hi,
+                                cudaStream_t s);
+cudaError_t launch_from_env_major(const uint8_t* src, uint8_t* dst, int rows, int S, int lo, int hi,
+                                  cudaStream_t s);
+}  // namespace gbx
+
+using namespace gbx;
+
+static_assert(GBX_I32_COUNT == I32_COUNT, "i32 field table mismatch");
+static_assert(GBX_I64_COUNT == I64_COUNT, "i64 field table mismatch");
+static_assert(GBX_U8_COUNT == U8_COUNT, "u8 field table mismatch");
+
+struct gbx_env {
+  DevState st;
+  gbx_config cfg;
+  int32_t ram_bytes;       // cartridge RAM bytes per env (0 if none)
+  int32_t ram_rows;        // max(ram_bytes, 1): rows allocated/snapshotted
+  uint8_t* pix;
+  uint8_t* pix_packed;
+  uint8_t* staging;        // device staging for layout conversion
+  size_t staging_bytes;
+  bool initialized;
+};
+
+struct gbx_snapshot {
+  Snapshot s;
+  void* block;
+  int device;
+};
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? GBX_ERR_OOM : GBX_ERR_CUDA, "%s: %s", what,
+              cudaGetErrorString(e));
+}
+
+#define CK(call, what)                          \
+  do {                                          \
+    cudaError_t e_ = (call);                    \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+inline cudaStream_t S_(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+const int kRomSizes[][2] = {{0x00, 32 << 10}, {0x01, 64 << 10}, {0x02, 128 << 10}, {0x03, 256 << 10},
+                            {0x04, 512 << 10}, {0x05, 1 << 20}, {0x06, 2 << 20}, {0x07, 4 << 20},
+                            {0x08, 8 << 20}, {0x52, 1153433}, {0x53, 1258291}, {0x54, 1572864}};
+const int kRamSizes[][2] = {{0x00, 0}, {0x01, 2 << 10}, {0x02, 8 << 10}, {0x03, 32 << 10},
+                            {0x04, 128 << 10}, {0x05, 64 << 10}};
+
+// src/gbxcule/core/cartridge.py:139-187
+int parse_header(const uint8_t* rom, size_t len, int* mbc, int* rom_bytes, int* ram_bytes) {
+  if (len < 0x150) return fail(GBX_ERR_INVALID, "ROM too small for header: %zu bytes", len);
+  int ct = rom[0x147];
+  if (ct == 0x00) *mbc = MBC_ROM_ONLY;
+  else if (ct >= 0x01 && ct <= 0x03) *mbc = MBC_MBC1;
+  else if (ct >= 0x0F && ct <= 0x13) *mbc = MBC_MBC3;
+  else return fail(GBX_ERR_INVALID, "Unsupported cartridge type: 0x%02X", ct);
+  *rom_bytes = -1;
+  for (auto& r : kRomSizes) if (r[0] == rom[0x148]) *rom_bytes = r[1];
+  if (*rom_bytes < 0) return fail(GBX_ERR_INVALID, "Unsupported ROM size code: 0x%02X", rom[0x148]);
+  if (*rom_bytes % ROM_BANK) return fail(GBX_ERR_INVALID, "Invalid ROM byte length: %d", *rom_bytes);
+  *ram_bytes = -1;
+  for (auto& r : kRamSizes) if (r[0] == rom[0x149]) *ram_bytes = r[1];
+  if (*ram_bytes < 0) return fail(GBX_ERR_INVALID, "Unsupported RAM size code: 0x%02X", rom[0x149]);
+  if (*ram_bytes % RAM_BANK) return fail(GBX_ERR_INVALID, "Invalid RAM byte length: %d", *ram_bytes);
+  if (len < (size_t)*rom_bytes)
+    return fail(GBX_ERR_INVALID, "ROM smaller than header advertises: %zu < %d", len, *rom_bytes);
+  return GBX_OK;
+}
+
+template <class T>
+int dalloc(T** p, size_t count) {
+  *p = nullptr;
+  if (count == 0) count = 1;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  return GBX_OK;
+}
+
+void free_env(gbx_env* h) {
+  DevState& st = h->st;
+  void* ptrs[] = {(void*)st.rom, (void*)st.boot, st.mem, st.cart_ram, st.serial, st.cart_state, st.i32,
+                  st.i64, st.u8s, st.latch, st.obs, st.reward, st.status, h->pix, h->pix_packed, h->staging};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+}
+
+int zero_state(gbx_env* h, cudaStream_t s) {
+  DevState& st = h->st;
+  const size_t S = st.S;
+  CK(cudaMemsetAsync(st.mem, 0, (size_t)MEM_SIZE * S, s), "memset mem");
+  CK(cudaMemsetAsync(st.cart_ram, 0, (size_t)h->ram_rows * S, s), "memset cart_ram");
+  CK(cudaMemsetAsync(st.serial, 0, (size_t)SERIAL_MAX * S, s), "memset serial");
+  CK(cudaMemsetAsync(st.cart_state, 0, sizeof(int32_t) * CS_STRIDE * S, s), "memset cart_state");
+  CK(cudaMemsetAsync(st.i32, 0, sizeof(int32_t) * I32_COUNT * S, s), "memset i32");
+  CK(cudaMemsetAsync(st.i64, 0, sizeof(int64_t) * I64_COUNT * S, s), "memset i64");
+  CK(cudaMemsetAsync(st.u8s, 0, (size_t)U8_COUNT * S, s), "memset u8");
+  CK(cudaMemsetAsync(st.latch, 0, 9 * SCREEN_H, s), "memset latch");
+  CK(cudaMemsetAsync(st.obs, 0, sizeof(float) * OBS_DIM * (size_t)st.n, s), "memset obs");
+  CK(cudaMemsetAsync(st.reward, 0, sizeof(float) * (size_t)st.n, s), "memset reward");
+  CK(cudaMemsetAsync(st.status, 0, sizeof(uint32_t), s), "memset status");
+  if (h->pix) CK(cudaMemsetAsync(h->pix, 0, (size_t)SHADE_BYTES * st.n, s), "memset pix");
+  if (h->pix_packed) CK(cudaMemsetAsync(h->pix_packed, 0, (size_t)PACKED_BYTES * st.n, s), "memset pix_packed");
+  return GBX_OK;
+}
+
+int check_env(const gbx_env* h) {
+  if (!h) return fail(GBX_ERR_INVALID, "null gbx_env");
+  return GBX_OK;
+}
+int check_init(const gbx_env* h) {
+  if (!h) return fail(GBX_ERR_INVALID, "null gbx_env");
+  if (!h->initialized) return fail(GBX_ERR_STATE, "Backend not initialized. Call reset() first.");
+  return GBX_OK;
+}
+int check_range(const gbx_env* h, int lo, int hi) {
+  if (lo < 0 || hi > h->st.n || lo > hi)
+    return fail(GBX_ERR_RANGE, "env range [%d, %d) out of range [0, %d)", lo, hi, h->st.n);
+  return GBX_OK;
+}
+
+// interleaved rows [rows][S] -> host env-major [hi-lo][rows], chunked through staging
+int export_rows(gbx_env* h, const uint8_t* src, int rows, int lo, int hi, uint8_t* host) {
+  const int per = (int)(h->staging_bytes / (size_t)rows);
+  for (int e = lo; e < hi; e += per) {
+    int e1 = e + per < hi ? e + per : hi;
+    CK(launch_to_env_major(src, h->staging, rows, h->st.S, e, e1, 0), "to_env_major");
+    CK(cudaMemcpy(host + (size_t)(e - lo) * rows, h->staging, (size_t)(e1 - e) * rows, cudaMemcpyDeviceToHost),
+       "export copy");
+  }
+  return GBX_OK;
+}
+int import_rows(gbx_env* h, uint8_t* dst, int rows, int lo, int hi, const uint8_t* host) {
+  const int per = (int)(h->staging_bytes / (size_t)rows);
+  for (int e = lo; e < hi; e += per) {
+    int e1 = e + per < hi ? e + per : hi;
+    CK(cudaMemcpy(h->staging, host + (size_t)(e - lo) * rows, (size_t)(e1 - e) * rows, cudaMemcpyHostToDevice),
+       "import copy");
+    CK(launch_from_env_major(h->staging, dst, rows, h->st.S, e, e1, 0), "from_env_major");
+  }
+  CK(cudaDeviceSynchronize(), "import sync");
+  return GBX_OK;
+}
+template <class T>
+int copy_fields(T* dev, int fields, size_t S, int lo, int hi, T* host, bool to_host) {
+  size_t w = sizeof(T) * (size_t)(hi - lo);
+  if (w == 0) return GBX_OK;
+  if (to_host)
+    CK(cudaMemcpy2D(host, w, dev + lo, sizeof(T) * S, w, fields, cudaMemcpyDeviceToHost), "field copy");
+  else
+    CK(cudaMemcpy2D(dev + lo, sizeof(T) * S, host, w, w, fields, cudaMemcpyHostToDevice), "field copy");
+  return GBX_OK;
+}
+
+}  // namespace
+
+#define RET(x)                     \
+  do {                             \
+    int r_ = (x);                  \
+    if (r_ != GBX_OK) return r_;   \
+  } while (0)
+
+extern "C" {
+
+int32_t gbx_abi_version(void) { return GBX_ABI_VERSION; }
+
+const char* gbx_last_error(void) { return g_err.c_str(); }
+
+int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const uint8_t* boot, size_t boot_len,
+               gbx_env** out) {
+  if (!cfg || !rom || !boot || !out) return fail(GBX_ERR_INVALID, "null argument to gbx_create");
+  *out = nullptr;
+  if (cfg->num_envs <= 0) return fail(GBX_ERR_INVALID, "num_envs must be > 0, got %d", cfg->num_envs);
+  if (cfg->stage < 0 || cfg->stage > 3) return fail(GBX_ERR_INVALID, "unknown stage %d", cfg->stage);
+  if (boot_len != 0x100) return fail(GBX_ERR_INVALID, "Boot ROM must be 256 bytes, got %zu", boot_len);
+  int mbc, rom_bytes, ram_bytes;
+  RET(parse_header(rom, rom_len, &mbc, &rom_bytes, &ram_bytes));
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || cfg->device < 0 || cfg->device >= ndev)
+    return fail(GBX_ERR_INVALID, "CUDA device %d not available (%d devices)", cfg->device, ndev);
+  DeviceGuard g(cfg->device);
+  gbx_env* h = new (std::nothrow) gbx_env();
+  if (!h) return fail(GBX_ERR_OOM, "host allocation failed");
+  memset(h, 0, sizeof *h);
+  h->cfg = *cfg;
+  DevState& st = h->st;
+  st.n = cfg->num_envs;
+  st.S = (cfg->num_envs + 127) & ~127;
+  st.mbc_kind = mbc;
+  st.rom_bytes = rom_bytes;
+  st.rom_bank_count = rom_bytes / ROM_BANK;
+  st.rom_bank_mask = (st.rom_bank_count & (st.rom_bank_count - 1)) == 0 ? st.rom_bank_count - 1 : -1;
+  st.ram_bank_count = ram_bytes / RAM_BANK;
+  h->ram_bytes = ram_bytes;
+  h->ram_rows = ram_bytes > 0 ? ram_bytes : 1;
+  const size_t S = st.S;
+  int rc = GBX_OK;
+  uint8_t *rom_d = nullptr, *boot_d = nullptr;
+  if ((rc = dalloc(&rom_d, (size_t)rom_bytes)) || (rc = dalloc(&boot_d, 256)) ||
+      (rc = dalloc(&st.mem, (size_t)MEM_SIZE * S)) || (rc = dalloc(&st.cart_ram, (size_t)h->ram_rows * S)) ||
+      (rc = dalloc(&st.serial, (size_t)SERIAL_MAX * S)) || (rc = dalloc(&st.cart_state, (size_t)CS_STRIDE * S)) ||
+      (rc = dalloc(&st.i32, (size_t)I32_COUNT * S)) || (rc = dalloc(&st.i64, (size_t)I64_COUNT * S)) ||
+      (rc = dalloc(&st.u8s, (size_t)U8_COUNT * S)) || (rc = dalloc(&st.latch, 9 * SCREEN_H)) ||
+      (rc = dalloc(&st.obs, (size_t)OBS_DIM * st.n)) || (rc = dalloc(&st.reward, (size_t)st.n)) ||
+      (rc = dalloc(&st.status, 1)) ||
+      (cfg->alloc_pixels && (rc = dalloc(&h->pix, (size_t)SHADE_BYTES * st.n))) ||
+      (cfg->alloc_pixels_packed && (rc = dalloc(&h->pix_packed, (size_t)PACKED_BYTES * st.n)))) {
+    st.rom = rom_d;
+    st.boot = boot_d;
+    free_env(h);
+    delete h;
+    return rc;
+  }
+  st.rom = rom_d;
+  st.boot = boot_d;
+  h->staging_bytes = (size_t)64 << 20;
+  if ((rc = dalloc(&h->staging, h->staging_bytes))) {
+    free_env(h);
+    delete h;
+    return rc;
+  }
+  cudaError_t e = cudaMemcpy(rom_d, rom, (size_t)rom_bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(boot_d, boot, 256, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    free_env(h);
+    delete h;
+    return cuda_fail(e, "upload ROM");
+  }
+  *out = h;
+  return GBX_OK;
+}
+
+int gbx_destroy(gbx_env* h) {
+  if (!h) return GBX_OK;
+  DeviceGuard g(h->cfg.device);
+  cudaDeviceSynchronize();
+  free_env(h);
+  delete h;
+  return GBX_OK;
+}
+
+int gbx_get_info(const gbx_env* h, gbx_info* out) {
+  RET(check_env(h));
+  if (!out) return fail(GBX_ERR_INVALID, "null out");
+  out->num_envs = h->st.n;
+  out->env_stride = h->st.S;
+  out->device = h->cfg.device;
+  out->stage = h->cfg.stage;
+  out->mbc_kind = h->st.mbc_kind;
+  out->rom_bytes = h->st.rom_bytes;
+  out->rom_bank_count = h->st.rom_bank_count;
+  out->rom_bank_mask = h->st.rom_bank_mask;
+  out->ram_bank_count = h->st.ram_bank_count;
+  out->ram_bytes = h->ram_bytes;
+  return GBX_OK;
+}
+
+int gbx_reset(gbx_env* h, void* stream) {
+  RET(check_env(h));
+  DeviceGuard g(h->cfg.device);
+  cudaStream_t s = S_(stream);
+  RET(zero_state(h, s));
+  CK(launch_init(h->st, s), "init kernel");
+  h->initialized = true;
+  if (h->cfg.stage == STAGE_OBS || h->cfg.stage == STAGE_FULL) {
+    const int32_t* zero_actions = h->st.i32 + (size_t)F_ACTIONS * h->st.S;
+    CK(launch_step(h->st, zero_actions, 0, 0, h->cfg.stage, s), "step kernel (reset obs)");
+  }
+  return GBX_OK;
+}
+
+int gbx_step(gbx_env* h, const int32_t* actions, int32_t frames, int32_t release, void* stream) {
+  RET(check_init(h));
+  if (!actions) return fail(GBX_ERR_INVALID, "actions is null");
+  if (frames < 0) return fail(GBX_ERR_INVALID, "frames_to_run must be >= 0, got %d", frames);
+  if (frames > 25000) return fail(GBX_ERR_INVALID, "frames_to_run %d exceeds 25000 per launch", frames);
+  DeviceGuard g(h->cfg.device);
+  CK(launch_step(h->st, actions, frames, release, h->cfg.stage, S_(stream)), "step kernel");
+  return GBX_OK;
+}
+
+int gbx_render_packed(gbx_env* h, uint8_t* out, int64_t base_offset, void* stream) {
+  RET(check_init(h));
+  if (base_offset < 0) return fail(GBX_ERR_INVALID, "base_offset_bytes must be >= 0");
+  if (!out) {
+    if (!h->pix_packed) return fail(GBX_ERR_STATE, "Packed pixel buffer not initialized. Call reset() first.");
+    out = h->pix_packed;
+    base_offset = 0;
+  }
+  DeviceGuard g(h->cfg.device);
+  CK(launch_render(h->st, out, base_offset, true, S_(stream)), "render kernel");
+  return GBX_OK;
+}
+
+int gbx_render_shades(gbx_env* h, uint8_t* out, void* stream) {
+  RET(check_init(h));
+  if (!out) {
+    if (!h->pix) return fail(GBX_ERR_STATE, "Pixel buffer not initialized. Call reset() first.");
+    out = h->pix;
+  }
+  DeviceGuard g(h->cfg.device);
+  CK(launch_render(h->st, out, 0, false, S_(stream)), "render kernel");
+  return GBX_OK;
+}
+
+int gbx_snapshot_create(gbx_env* h, int32_t env_idx, void* stream, gbx_snapshot** out) {
+  RET(check_init(h));
+  if (!out) return fail(GBX_ERR_INVALID, "null out");
+  *out = nullptr;
+  if (env_idx < 0 || env_idx >= h->st.n)
+    return fail(GBX_ERR_RANGE, "env_idx %d out of range [0, %d)", env_idx, h->st.n);
+  DeviceGuard g(h->cfg.device);
+  gbx_snapshot* sn = new (std::nothrow) gbx_snapshot();
+  if (!sn) return fail(GBX_ERR_OOM, "host allocation failed");
+  const size_t bytes = (size_t)MEM_SIZE + h->ram_rows + SERIAL_MAX + 4 * CS_STRIDE + 4 * I32_COUNT + 8 * I64_COUNT +
+                       U8_COUNT + 64;
+  cudaError_t e = cudaMalloc(&sn->block, bytes);
+  if (e != cudaSuccess) {
+    delete sn;
+    return cuda_fail(e, "snapshot alloc");
+  }
+  uint8_t* p = static_cast<uint8_t*>(sn->block);
+  sn->s.i64 = reinterpret_cast<int64_t*>(p); p += 8 * I64_COUNT;
+  sn->s.cart_state = reinterpret_cast<int32_t*>(p); p += 4 * CS_STRIDE;
+  sn->s.i32 = reinterpret_cast<int32_t*>(p); p += 4 * I32_COUNT;
+  sn->s.u8s = p; p += U8_COUNT;
+  sn->s.mem = p; p += MEM_SIZE;
+  sn->s.serial = p; p += SERIAL_MAX;
+  sn->s.cart_ram = p;
+  sn->s.ram_bytes = h->ram_rows;
+  sn->device = h->cfg.device;
+  e = launch_snapshot(h->st, sn->s, env_idx, S_(stream));
+  if (e != cudaSuccess) {
+    cudaFree(sn->block);
+    delete sn;
+    return cuda_fail(e, "snapshot kernel");
+  }
+  *out = sn;
+  return GBX_OK;
+}
+
+int gbx_snapshot_destroy(gbx_snapshot* sn) {
+  if (!sn) return GBX_OK;
+  DeviceGuard g(sn->device);
+  cudaDeviceSynchronize();
+  cudaFree(sn->block);
+  delete sn;
+  return GBX_OK;
+}
+
+int gbx_masked_restore(gbx_env* h, const gbx_snapshot* sn, const uint8_t* mask, void* stream) {
+  RET(check_init(h));
+  if (!sn || !mask) return fail(GBX_ERR_INVALID, "null snapshot or mask");
+  if (sn->device != h->cfg.device || sn->s.ram_bytes != h->ram_rows)
+    return fail(GBX_ERR_INVALID, "snapshot belongs to a different env batch");
+  DeviceGuard g(h->cfg.device);
+  CK(launch_restore(h->st, sn->s, mask, S_(stream)), "restore kernel");
+  return GBX_OK;
+}
+
+int gbx_buffer(const gbx_env* h, int32_t which, gbx_buffer_info* o) {
+  RET(check_env(h));
+  if (!o) return fail(GBX_ERR_INVALID, "null out");
+  memset(o, 0, sizeof *o);
+  const DevState& st = h->st;
+  const int64_t n = st.n, S = st.S;
+  auto set = [&](void* d, int code, int bits, int nd, int64_t s0, int64_t s1, int64_t s2, int64_t t0, int64_t t1,
+                 int64_t t2) {
+    o->data = d; o->dtype_code = code; o->dtype_bits = bits; o->ndim = nd;
+    o->shape[0] = s0; o->shape[1] = s1; o->shape[2] = s2;
+    o->strides[0] = t0; o->strides[1] = t1; o->strides[2] = t2;
+  };
+  switch (which) {
+    case GBX_BUF_MEM: set(st.mem, 1, 8, 2, n, MEM_SIZE, 0, 1, S, 0); break;
+    case GBX_BUF_PIXELS:
+      if (!h->pix) return fail(GBX_ERR_STATE, "Pixel buffer not initialized. Call reset() first.");
+      set(h->pix, 1, 8, 3, n, 72, 80, SHADE_BYTES, 80, 1); break;
+    case GBX_BUF_PIXELS_PACKED:
+      if (!h->pix_packed) return fail(GBX_ERR_STATE, "Packed pixel buffer not initialized. Call reset() first.");
+      set(h->pix_packed, 1, 8, 3, n, 72, 20, PACKED_BYTES, 20, 1); break;
+    case GBX_BUF_OBS: set(st.obs, 2, 32, 2, n, OBS_DIM, 0, OBS_DIM, 1, 0); break;
+    case GBX_BUF_REWARD: set(st.reward, 2, 32, 1, n, 0, 0, 1, 0, 0); break;
+    case GBX_BUF_CART_RAM: set(st.cart_ram, 1, 8, 2, n, h->ram_rows, 0, 1, S, 0); break;
+    case GBX_BUF_SERIAL: set(st.serial, 1, 8, 2, n, SERIAL_MAX, 0, 1, S, 0); break;
+    case GBX_BUF_I32: set(st.i32, 0, 32, 2, I32_COUNT, n, 0, S, 1, 0); break;
+    case GBX_BUF_I64: set(st.i64, 0, 64, 2, I64_COUNT, n, 0, S, 1, 0); break;
+    case GBX_BUF_U8: set(st.u8s, 1, 8, 2, U8_COUNT, n, 0, S, 1, 0); break;
+    case GBX_BUF_CART_STATE: set(st.cart_state, 0, 32, 2, CS_STRIDE, n, 0, S, 1, 0); break;
+    case GBX_BUF_LATCH: set(st.latch, 1, 8, 2, 9, SCREEN_H, 0, SCREEN_H, 1, 0); break;
+    default: return fail(GBX_ERR_INVALID, "unknown buffer id %d", which);
+  }
+  return GBX_OK;
+}
+
+static void dl_deleter(DLManagedTensor* t) { free(t); }
+
+int gbx_export_dlpack(const gbx_env* h, int32_t which, void** out) {
+  if (!out) return fail(GBX_ERR_INVALID, "null out");
+  *out = nullptr;
+  gbx_buffer_info b;
+  RET(gbx_buffer(h, which, &b));
+  // one block: tensor, then shape[3], strides[3]
+  DLManagedTensor* t = static_cast<DLManagedTensor*>(malloc(sizeof(DLManagedTensor) + 6 * sizeof(int64_t)));
+  if (!t) return fail(GBX_ERR_OOM, "host allocation failed");
+  int64_t* shape = reinterpret_cast<int64_t*>(t + 1);
+  int64_t* strides = shape + 3;
+  for (int k = 0; k < 3; k++) { shape[k] = b.shape[k]; strides[k] = b.strides[k]; }
+  t->dl_tensor.data = b.data;
+  t->dl_tensor.device.device_type = 2;  // kDLCUDA
+  t->dl_tensor.device.device_id = h->cfg.device;
+  t->dl_tensor.ndim = b.ndim;
+  t->dl_tensor.dtype.code = (uint8_t)b.dtype_code;
+  t->dl_tensor.dtype.bits = (uint8_t)b.dtype_bits;
+  t->dl_tensor.dtype.lanes = 1;
+  t->dl_tensor.shape = shape;
+  t->dl_tensor.strides = strides;
+  t->dl_tensor.byte_offset = 0;
+  t->manager_ctx = nullptr;
+  t->deleter = dl_deleter;
+  *out = t;
+  return GBX_OK;
+}
+
+int gbx_export_state(gbx_env* h, int32_t lo, int32_t hi, const gbx_host_state* o) {
+  RET(check_init(h));
+  RET(check_range(h, lo, hi));
+  if (!o) return fail(GBX_ERR_INVALID, "null out");
+  DeviceGuard g(h->cfg.device);
+  CK(cudaDeviceSynchronize(), "sync before export");
+  const DevState& st = h->st;
+  const size_t S = st.S;
+  if (o->mem) RET(export_rows(h, st.mem, MEM_SIZE, lo, hi, o->mem));
+  if (o->cart_ram) RET(export_rows(h, st.cart_ram, h->ram_rows, lo, hi, o->cart_ram));
+  if (o->serial) RET(export_rows(h, st.serial, SERIAL_MAX, lo, hi, o->serial));
+  if (o->cart_state) RET(copy_fields(st.cart_state, CS_STRIDE, S, lo, hi, o->cart_state, true));
+  if (o->i32) RET(copy_fields(st.i32, I32_COUNT, S, lo, hi, o->i32, true));
+  if (o->i64) RET(copy_fields(st.i64, I64_COUNT, S, lo, hi, o->i64, true));
+  if (o->u8s) RET(copy_fields(st.u8s, U8_COUNT, S, lo, hi, o->u8s, true));
+  if (o->latch) CK(cudaMemcpy(o->latch, st.latch, 9 * SCREEN_H, cudaMemcpyDeviceToHost), "latch copy");
+  if (o->obs && hi > lo)
+    CK(cudaMemcpy(o->obs, st.obs + (size_t)lo * OBS_DIM, sizeof(float) * OBS_DIM * (hi - lo), cudaMemcpyDeviceToHost),
+       "obs copy");
+  if (o->reward && hi > lo)
+    CK(cudaMemcpy(o->reward, st.reward + lo, sizeof(float) * (hi - lo), cudaMemcpyDeviceToHost), "reward copy");
+  return GBX_OK;
+}
+
+int gbx_import_state(gbx_env* h, int32_t lo, int32_t hi, const gbx_host_state* in) {
+  RET(check_init(h));
+  RET(check_range(h, lo, hi));
+  if (!in) return fail(GBX_ERR_INVALID, "null in");
+  DeviceGuard g(h->cfg.device);
+  CK(cudaDeviceSynchronize(), "sync before import");
+  const DevState& st = h->st;
+  const size_t S = st.S;
+  if (in->mem) RET(import_rows(h, st.mem, MEM_SIZE, lo, hi, in->mem));
+  if (in->cart_ram) RET(import_rows(h, st.cart_ram, h->ram_rows, lo, hi, in->cart_ram));
+  if (in->serial) RET(import_rows(h, st.serial, SERIAL_MAX, lo, hi, in->serial));
+  if (in->cart_state) RET(copy_fields(st.cart_state, CS_STRIDE, S, lo, hi, in->cart_state, false));
+  if (in->i32) RET(copy_fields(st.i32, I32_COUNT, S, lo, hi, in->i32, false));
+  if (in->i64) RET(copy_fields(st.i64, I64_COUNT, S, lo, hi, in->i64, false));
+  if (in->u8s) RET(copy_fields(st.u8s, U8_COUNT, S, lo, hi, in->u8s, false));
+  if (in->latch) CK(cudaMemcpy(st.latch, in->latch, 9 * SCREEN_H, cudaMemcpyHostToDevice), "latch copy");
+  if (in->obs && hi > lo)
+    CK(cudaMemcpy(st.obs + (size_t)lo * OBS_DIM, in->obs, sizeof(float) * OBS_DIM * (hi - lo), cudaMemcpyHostToDevice),
+       "obs copy");
+  if (in->reward && hi > lo)
+    CK(cudaMemcpy(st.reward + lo, in->reward, sizeof(float) * (hi - lo), cudaMemcpyHostToDevice), "reward copy");
+  CK(cudaDeviceSynchronize(), "sync after import");
+  return GBX_OK;
+}
+
+int gbx_read_mem(gbx_env* h, int32_t env_idx, int32_t lo, int32_t hi, uint8_t* host_out) {
+  RET(check_init(h));
+  if (env_idx < 0 || env_idx >= h->st.n)
+    return fail(GBX_ERR_RANGE, "env_idx %d out of range [0, %d)", env_idx, h->st.n);
+  if (lo < 0 || hi < 0 || lo > MEM_SIZE || hi > MEM_SIZE || lo > hi)
+    return fail(GBX_ERR_RANGE, "Invalid memory range: lo=%d hi=%d", lo, hi);
+  if (hi == lo) return GBX_OK;
+  if (!host_out) return fail(GBX_ERR_INVALID, "null out");
+  DeviceGuard g(h->cfg.device);
+  CK(cudaDeviceSynchronize(), "sync before read");
+  const uint8_t* src = h->st.mem + (size_t)lo * h->st.S;
+  CK(launch_to_env_major(src, h->staging, hi - lo, h->st.S, env_idx, env_idx + 1, 0), "to_env_major");
+  CK(cudaMemcpy(host_out, h->staging, (size_t)(hi - lo), cudaMemcpyDeviceToHost), "read copy");
+  return GBX_OK;
+}
+
+int gbx_status(gbx_env* h, uint32_t* out, int32_t clear) {
+  RET(check_env(h));
+  if (!out) return fail(GBX_ERR_INVALID, "null out");
+  DeviceGuard g(h->cfg.device);
+  CK(cudaDeviceSynchronize(), "sync before status");
+  CK(cudaMemcpy(out, h->st.status, sizeof(uint32_t), cudaMemcpyDeviceToHost), "status copy");
+  if (clear) CK(cudaMemset(h->st.status, 0, sizeof(uint32_t)), "status clear");
+  return GBX_OK;
+}
+
+}  // extern "C"

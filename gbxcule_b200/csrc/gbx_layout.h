@@ -1,0 +1,96 @@
+// gbx_layout.h - device-side data layout shared by every kernel of libgbx.
+//
+// HBM layout (one allocation set per handle, S = env stride, a multiple of 32):
+//   mem        u8  [65536][S]  byte a of env e at mem[a*S + e] (address-major,
+//                               env-minor: a warp touching one address reads
+//                               one 32-byte sector)
+//   cart_ram   u8  [ram_bytes][S]       same interleaving
+//   serial     u8  [1024][S]
+//   cart_state i32 [20][S]              field-major (SoA)
+//   i32        i32 [I32_COUNT][S]       one row per scalar field (SoA)
+//   i64        i64 [2][S]               instr_count, cycle_count
+//   u8s        u8  [U8_COUNT][S]        joyp_select, serial_overflow, stat_prev
+//   latch      u8  [9][144]             env-0 scanline latches
+//   obs        f32 [N][32], reward f32 [N]   (reference layout, torch views)
+//   pix_packed u8  [N][72][20], pix u8 [N][72][80]
+// The reference keeps the same fields env-major (warp_vec.py:279-497); the
+// host API converts when it exports state.
+#pragma once
+#include <stdint.h>
+
+namespace gbx {
+
+constexpr int MEM_SIZE = 65536;
+constexpr int CYCLES_PER_FRAME = 70224;
+constexpr int CYCLES_PER_LINE = 456;
+constexpr int LINES_PER_FRAME = 154;
+constexpr int SCREEN_H = 144;
+constexpr int ROM_BANK = 0x4000;
+constexpr int RAM_BANK = 0x2000;
+constexpr int SERIAL_MAX = 1024;
+constexpr int OBS_DIM = 32;
+constexpr int CS_STRIDE = 20;
+constexpr int RTC_CPS = 4194304;
+constexpr int PACKED_BYTES = 72 * 20;   // 1440 per env
+constexpr int SHADE_BYTES = 72 * 80;    // 5760 per env
+constexpr int ROM_SMEM_MAX = 0x8000;    // banks 0-1 staged in shared memory
+
+enum MbcKind { MBC_ROM_ONLY = 0, MBC_MBC1 = 1, MBC_MBC3 = 2 };
+enum Stage { STAGE_EMULATE = 0, STAGE_OBS = 1, STAGE_REWARD = 2, STAGE_FULL = 3 };
+
+// cart_state record (src/gbxcule/core/cartridge.py:56-76)
+enum CartField {
+  CS_MBC_KIND, CS_RAM_ENABLE, CS_ROM_BANK_LO, CS_ROM_BANK_HI, CS_RAM_BANK, CS_BANK_MODE,
+  CS_BOOTROM, CS_RTC_SELECT, CS_RTC_LATCH, CS_RTC_S, CS_RTC_M, CS_RTC_H, CS_RTC_DL,
+  CS_RTC_DH, CS_RTC_LAST, CS_RTC_LS, CS_RTC_LM, CS_RTC_LH, CS_RTC_LDL, CS_RTC_LDH
+};
+
+// i32 SoA rows
+enum I32Field {
+  F_PC, F_SP, F_A, F_B, F_C, F_D, F_E, F_H, F_L, F_F,
+  F_CYCLE_IN_FRAME, F_TRAP_FLAG, F_TRAP_PC, F_TRAP_OPCODE, F_TRAP_KIND,
+  F_SERIAL_LEN, F_IME, F_IME_DELAY, F_HALTED, F_DIV_COUNTER, F_TIMER_PREV_IN,
+  F_TIMA_RELOAD_PENDING, F_TIMA_RELOAD_DELAY, F_PPU_SCANLINE_CYCLE, F_PPU_LY,
+  F_PPU_WINDOW_LINE, F_ACTIONS, I32_COUNT
+};
+enum I64Field { F_INSTR_COUNT, F_CYCLE_COUNT, I64_COUNT };
+enum U8Field { F_JOYP_SELECT, F_SERIAL_OVERFLOW, F_STAT_PREV, U8_COUNT };
+
+// device status bits (OR-ed into DevState::status)
+enum StatusBits {
+  STATUS_MBC_MISMATCH = 1,   // an env's cart_state mbc_kind differs from the cart's
+  STATUS_BAD_ARGS = 2,
+};
+
+struct DevState {
+  const uint8_t* rom;     // [rom_bytes] shared, read-only
+  const uint8_t* boot;    // [256]
+  int32_t rom_bytes, rom_bank_count, rom_bank_mask, ram_bank_count;
+  int32_t n, S;           // envs, env stride
+  int32_t mbc_kind;
+  uint8_t* mem;
+  uint8_t* cart_ram;
+  uint8_t* serial;
+  int32_t* cart_state;
+  int32_t* i32;
+  int64_t* i64;
+  uint8_t* u8s;
+  uint8_t* latch;
+  float* obs;
+  float* reward;
+  uint32_t* status;
+};
+
+// Device-resident copy of one env (ResetCache, src/gbxcule/core/reset_cache.py:22-64).
+struct Snapshot {
+  uint8_t* mem;         // [65536]
+  uint8_t* cart_ram;    // [ram_bytes] (>= 1)
+  uint8_t* serial;      // [1024]
+  int32_t* cart_state;  // [20]
+  int32_t* i32;         // [I32_COUNT]
+  int64_t* i64;         // [I64_COUNT]
+  uint8_t* u8s;         // [U8_COUNT]
+  int32_t ram_bytes;
+};
+
+}  // namespace gbx
