@@ -29,9 +29,9 @@ cudaError_t launch_from_env_major(const uint8_t* src, uint8_t* dst, int rows, in
 
 using namespace gbx;
 
-static_assert(GBX_I32_COUNT == I32_COUNT, "i32 field table mismatch");
-static_assert(GBX_I64_COUNT == I64_COUNT, "i64 field table mismatch");
-static_assert(GBX_U8_COUNT == U8_COUNT, "u8 field table mismatch");
+static_assert((int)GBX_I32_COUNT == (int)I32_COUNT, "i32 field table mismatch");
+static_assert((int)GBX_I64_COUNT == (int)I64_COUNT, "i64 field table mismatch");
+static_assert((int)GBX_U8_COUNT == (int)U8_COUNT, "u8 field table mismatch");
 
 struct gbx_env {
   DevState st;
@@ -535,7 +535,7 @@ int gbx_read_mem(gbx_env* h, int32_t env_idx, int32_t lo, int32_t hi, uint8_t* h
   return GBX_OK;
 }
 
-int gbx_status(gbx_env* h, uint32_t* out, int32_t clear) {
+int gbx_device_status(gbx_env* h, uint32_t* out, int32_t clear) {
   RET(check_env(h));
   if (!out) return fail(GBX_ERR_INVALID, "null out");
   DeviceGuard g(h->cfg.device);

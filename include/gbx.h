@@ -177,7 +177,7 @@ int gbx_read_mem(gbx_env* env, int32_t env_idx, int32_t lo, int32_t hi, uint8_t*
 
 /* Device status word (bit 1: an env's cart_state mbc_kind differs from the
  * cartridge's); synchronous. Optionally clears it. */
-int gbx_status(gbx_env* env, uint32_t* out, int32_t clear);
+int gbx_device_status(gbx_env* env, uint32_t* out, int32_t clear);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,267 @@
+"""Bit-exact parity of the CUDA path (libgbx via the backend) on a B200.
+
+* every golden case (digests from the reference's own source) replayed through
+  ``GbxVecCudaBackend`` / ``ResetCache``;
+* CUDA vs the CPU oracle on the five config ROMs at larger env counts, full
+  state every step;
+* the benchmark-size configs (4,096 / 16,384 / 65,536 envs) with a seeded
+  sample of envs replayed on the oracle from the same start state.
+"""
+
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+from gbxcule_b200 import roms
+from gbxcule_b200 import state as st
+from oracle import OracleEnvs
+from tests.conftest import case_rom
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _sha(b: bytes) -> str:
+    return hashlib.sha256(b).hexdigest()
+
+
+def _cases():
+    import json
+    from tests.conftest import GOLDEN
+
+    return json.loads((GOLDEN / "fixtures.json").read_text())["cases"]
+
+
+def _backend(rom, n, frames, release, stage="obs_only", **kw):
+    from gbxcule_b200 import GbxVecCudaBackend
+
+    be = GbxVecCudaBackend(rom, num_envs=n, frames_per_step=frames, release_after_frames=release,
+                           stage=stage, **kw)
+    be.reset()
+    return be
+
+
+def _step(be, actions):
+    be.step_torch(torch.as_tensor(np.asarray(actions, dtype=np.int32), device="cuda"))
+
+
+@pytest.mark.parametrize("case", _cases(), ids=lambda c: c["name"])
+def test_golden_case_on_gpu(case, micro_roms):
+    from gbxcule_b200 import ResetCache
+
+    rom = case_rom(case, micro_roms)
+    n = case["num_envs"]
+    be = _backend(rom, n, case["frames"], case["release"], case["stage"], render_pixels=True,
+                  render_pixels_packed=True, render_on_step=False)
+    try:
+        assert st.digest(be.export_state()) == case["reset_digest"]
+        trace, warm = case["trace"], case.get("warmup", 0)
+        for rec in trace[:warm]:
+            _step(be, rec["actions"])
+            assert st.digest(be.export_state()) == rec["digest"]
+        cache = None
+        if "restore" in case:
+            rs = case["restore"]
+            cache = ResetCache.from_backend(be, env_idx=rs["snapshot_env"])
+            cache.apply_mask_torch(torch.ones(n, dtype=torch.bool, device="cuda"))
+            assert st.digest(be.export_state()) == rs["after_full_restore"]
+        for k, rec in enumerate(trace[warm:]):
+            _step(be, rec["actions"])
+            assert st.digest(be.export_state()) == rec["digest"], f"step {k}"
+            if "render_packed" in rec:
+                be.render_pixels_snapshot_torch()
+                torch.cuda.synchronize()
+                assert _sha(be.pixels_packed_torch().cpu().numpy().tobytes()) == rec["render_packed"]
+                assert _sha(be.pixels_torch().cpu().numpy().tobytes()) == rec["render_shades"]
+            if "mask" in rec:
+                cache.apply_mask_torch(torch.tensor(rec["mask"], dtype=torch.uint8, device="cuda"))
+                assert st.digest(be.export_state()) == rec["after_restore"], f"restore step {k}"
+    finally:
+        be.close()
+
+
+CONFIG_RUNS = [  # (config, envs, steps, frames, release, action kind)
+    (1, 64, 6, 24, 8, "uniform9"),
+    (2, 256, 6, 24, 8, "uniform9"),
+    (3, 256, 5, 24, 8, "bernoulli"),
+    (4, 128, 4, 24, 8, "uniform9"),
+    (5, 64, 4, 24, 8, "uniform9"),
+    (1, 37, 5, 3, 1, "uniform9"),     # ragged env count, short frames
+]
+
+
+def _acts(kind, rng, n):
+    return roms.bernoulli_actions(rng, n) if kind == "bernoulli" else roms.uniform_actions(rng, n, 9)
+
+
+@pytest.mark.parametrize("cfg,n,steps,frames,release,kind", CONFIG_RUNS)
+def test_cuda_matches_oracle(cfg, n, steps, frames, release, kind):
+    rom = roms.CONFIG_ROMS[cfg]()
+    be = _backend(rom, n, frames, release, render_pixels_packed=True, render_on_step=True)
+    o = OracleEnvs(rom, roms.boot_stub(), n)
+    rng = np.random.default_rng(100 + cfg)
+    try:
+        for k in range(steps):
+            a = _acts(kind, rng, n)
+            _step(be, a)
+            o.step(a, frames, release)
+            d = st.diff(be.export_state(), o.state(), n)
+            assert not d, f"config {cfg} step {k}: {d}"
+            torch.cuda.synchronize()
+            assert np.array_equal(be.pixels_packed_torch().cpu().numpy(), o.render_packed()), f"render step {k}"
+    finally:
+        be.close()
+
+
+def _export_sample(be, sample):
+    """Canonical state of the sampled envs, concatenated in sample order."""
+    parts = [be.export_state(int(e), int(e) + 1) for e in sample]
+    return {name: np.concatenate([np.asarray(p[name]).reshape(-1) for p in parts])
+            for name in st.ORDER if not name.startswith("latch_")}
+
+
+def _load_sample(be, o, sample):
+    got = _export_sample(be, sample)
+    for name, arr in got.items():
+        o.s[name][:] = arr
+
+
+FULL = [  # benchmark-size workloads: (config, envs, steps, action kind, restore rate)
+    (2, 4096, 3, "uniform9", 0.0),
+    (3, 16384, 2, "bernoulli", 0.0),
+    (4, 65536, 2, "uniform9", 0.05),
+]
+
+
+@pytest.mark.parametrize("cfg,n,steps,kind,rate", FULL)
+def test_full_size_sampled_envs_match_oracle(cfg, n, steps, kind, rate):
+    """Sampled envs of a full-size run replayed on the oracle, bit for bit."""
+    from gbxcule_b200 import ResetCache
+
+    rom = roms.CONFIG_ROMS[cfg]()
+    be = _backend(rom, n, 24, 8, render_pixels_packed=True, render_on_step=True)
+    rng = np.random.default_rng(1000 + cfg)
+    sample = np.sort(rng.choice(n, size=24, replace=False))
+    try:
+        cache = None
+        if rate > 0:
+            # warm up, then restore everyone from env 0's snapshot (config 4 protocol)
+            for _ in range(2):
+                _step(be, _acts(kind, rng, n))
+            cache = ResetCache.from_backend(be, env_idx=0)
+            cache.apply_mask_torch(torch.ones(n, dtype=torch.bool, device="cuda"))
+        o = OracleEnvs(rom, roms.boot_stub(), len(sample))
+        _load_sample(be, o, sample)
+        snap_o = o.snapshot(0)
+        for k in range(steps):
+            a = _acts(kind, rng, n)
+            _step(be, a)
+            o.step(a[sample], 24, 8)
+            if rate > 0:
+                mask = (np.random.default_rng(2000 + k).random(n) < rate)
+                cache.apply_mask_torch(torch.as_tensor(mask, device="cuda"))
+                o.restore(snap_o, mask[sample].astype(np.uint8))
+            got = _export_sample(be, sample)
+            for name in st.ORDER:
+                if name.startswith("latch_"):
+                    continue
+                assert np.array_equal(got[name], o.s[name]), f"config {cfg} step {k} field {name}"
+            torch.cuda.synchronize()
+            pix = be.pixels_packed_torch().cpu().numpy()[sample]
+            assert np.array_equal(pix, o.render_packed()), f"render step {k}"
+    finally:
+        be.close()
+
+
+def test_determinism_and_zero_copy_views():
+    """Two identical runs agree; torch views alias device state."""
+    rom = roms.config2_rom()
+    n = 512
+    a = _backend(rom, n, 24, 8, render_pixels_packed=True)
+    b = _backend(rom, n, 24, 8, render_pixels_packed=True)
+    try:
+        rng = np.random.default_rng(5)
+        for _ in range(3):
+            act = roms.uniform_actions(rng, n)
+            _step(a, act)
+            _step(b, act)
+        assert st.digest(a.export_state()) == st.digest(b.export_state())
+        mem = a.memory_torch()
+        assert tuple(mem.shape) == (n, 65536)
+        exp = a.export_state()["mem"].reshape(n, 65536)
+        assert np.array_equal(mem[:, 0x8000:].cpu().numpy(), exp[:, 0x8000:])
+        assert a.read_memory(3, 0xC000, 0xC010) == exp[3, 0xC000:0xC010].tobytes()
+        assert a.read_memory(3, 0x0000, 0x0200)[:0x100] == roms.boot_stub()
+        s = a.get_cpu_state(7)
+        assert s["pc"] == int(a.export_state(7, 8)["pc"][0])
+        assert a.device_status() == 0
+        # writes through the view reach the device state
+        mem[5, 0xC123] = 0xAB
+        torch.cuda.synchronize()
+        assert a.read_memory(5, 0xC123, 0xC124) == b"\xab"
+    finally:
+        a.close()
+        b.close()
+
+
+def test_api_errors_match_reference():
+    from gbxcule_b200 import GbxVecCudaBackend, ResetCache
+
+    rom = roms.config1_rom()
+    be = GbxVecCudaBackend(rom, num_envs=8)
+    with pytest.raises(RuntimeError, match="Call reset"):
+        be.step_torch(torch.zeros(8, dtype=torch.int32, device="cuda"))
+    be.reset()
+    with pytest.raises(ValueError, match="out of range"):
+        be.step(np.full(8, 9, dtype=np.int32))
+    with pytest.raises(ValueError, match="int32"):
+        be.step_torch(torch.zeros(8, dtype=torch.int64, device="cuda"))
+    with pytest.raises(ValueError, match="shape"):
+        be.step_torch(torch.zeros(7, dtype=torch.int32, device="cuda"))
+    with pytest.raises(TypeError):
+        be.step_torch(np.zeros(8, dtype=np.int32))
+    with pytest.raises(ValueError, match="CUDA"):
+        be.step_torch(torch.zeros(8, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        be.get_cpu_state(8)
+    with pytest.raises(ValueError, match="Invalid memory range"):
+        be.read_memory(0, 10, 5)
+    with pytest.raises(NotImplementedError):
+        be.write_memory(0, 0xC000, b"\x00")
+    out = torch.zeros(8 * 1440 - 1, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError, match="capacity"):
+        be.render_pixels_snapshot_packed_to_torch(out)
+    cache = ResetCache.from_backend(be)
+    with pytest.raises(ValueError, match="bool or uint8"):
+        cache.apply_mask_torch(torch.zeros(8, dtype=torch.int32, device="cuda"))
+    obs, rew, done, trunc, info = be.step(np.zeros(8, dtype=np.int32))
+    assert obs.shape == (8, 32) and obs.dtype == np.float32
+    be.close()
+    be.close()
+    with pytest.raises(RuntimeError):
+        be.memory_torch()
+
+
+def test_render_into_offset_buffer_matches_oracle():
+    rom = roms.config5_rom()
+    n = 40
+    be = _backend(rom, n, 24, 8)
+    o = OracleEnvs(rom, roms.boot_stub(), n)
+    rng = np.random.default_rng(9)
+    try:
+        for _ in range(3):
+            a = roms.uniform_actions(rng, n)
+            _step(be, a)
+            o.step(a, 24, 8)
+        for off in (0, 3, 16):
+            out = torch.zeros(off + n * 1440 + 5, dtype=torch.uint8, device="cuda")
+            be.render_pixels_snapshot_packed_to_torch(out, base_offset_bytes=off)
+            torch.cuda.synchronize()
+            got = out[off:off + n * 1440].cpu().numpy().reshape(n, 72, 20)
+            assert np.array_equal(got, o.render_packed())
+            assert int(out[:off].sum()) == 0 and int(out[off + n * 1440:].sum()) == 0
+    finally:
+        be.close()
