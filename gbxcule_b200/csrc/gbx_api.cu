@@ -14,8 +14,9 @@
 #include "gbx_layout.h"
 
 namespace gbx {
-cudaError_t launch_step(const DevState& st, const int32_t* actions, int frames, int release, int stage,
-                        cudaStream_t stream);
+cudaError_t launch_step(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames, int release,
+                        int stage, cudaStream_t stream);
+void predecode_rom(const uint8_t* rom, int n, uint32_t* out);
 cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
                           cudaStream_t stream);
 cudaError_t launch_init(const DevState& st, cudaStream_t s);
@@ -40,6 +41,7 @@ struct gbx_env {
   int32_t ram_rows;        // max(ram_bytes, 1): rows allocated/snapshotted
   uint8_t* pix;
   uint8_t* pix_packed;
+  uint32_t* pre;           // pre-decoded ROM, one word per byte (gbx_step.cu)
   uint8_t* staging;        // device staging for layout conversion
   size_t staging_bytes;
   bool initialized;
@@ -129,7 +131,8 @@ int dalloc(T** p, size_t count) {
 void free_env(gbx_env* h) {
   DevState& st = h->st;
   void* ptrs[] = {(void*)st.rom, (void*)st.boot, st.mem, st.cart_ram, st.serial, st.cart_state, st.i32,
-                  st.i64, st.u8s, st.latch, st.obs, st.reward, st.status, h->pix, h->pix_packed, h->staging};
+                  st.i64, st.u8s, st.latch, st.obs, st.reward, st.status, h->pix, h->pix_packed, h->staging,
+                  h->pre};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -268,8 +271,22 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
     delete h;
     return rc;
   }
+  if ((rc = dalloc(&h->pre, (size_t)rom_bytes))) {
+    free_env(h);
+    delete h;
+    return rc;
+  }
+  uint32_t* pre_host = new (std::nothrow) uint32_t[rom_bytes];
+  if (!pre_host) {
+    free_env(h);
+    delete h;
+    return fail(GBX_ERR_OOM, "host allocation failed");
+  }
+  predecode_rom(rom, rom_bytes, pre_host);
   cudaError_t e = cudaMemcpy(rom_d, rom, (size_t)rom_bytes, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(boot_d, boot, 256, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(h->pre, pre_host, sizeof(uint32_t) * rom_bytes, cudaMemcpyHostToDevice);
+  delete[] pre_host;
   if (e != cudaSuccess) {
     free_env(h);
     delete h;
@@ -313,7 +330,7 @@ int gbx_reset(gbx_env* h, void* stream) {
   h->initialized = true;
   if (h->cfg.stage == STAGE_OBS || h->cfg.stage == STAGE_FULL) {
     const int32_t* zero_actions = h->st.i32 + (size_t)F_ACTIONS * h->st.S;
-    CK(launch_step(h->st, zero_actions, 0, 0, h->cfg.stage, s), "step kernel (reset obs)");
+    CK(launch_step(h->st, h->pre, zero_actions, 0, 0, h->cfg.stage, s), "step kernel (reset obs)");
   }
   return GBX_OK;
 }
@@ -324,7 +341,7 @@ int gbx_step(gbx_env* h, const int32_t* actions, int32_t frames, int32_t release
   if (frames < 0) return fail(GBX_ERR_INVALID, "frames_to_run must be >= 0, got %d", frames);
   if (frames > 25000) return fail(GBX_ERR_INVALID, "frames_to_run %d exceeds 25000 per launch", frames);
   DeviceGuard g(h->cfg.device);
-  CK(launch_step(h->st, actions, frames, release, h->cfg.stage, S_(stream)), "step kernel");
+  CK(launch_step(h->st, h->pre, actions, frames, release, h->cfg.stage, S_(stream)), "step kernel");
   return GBX_OK;
 }
 

@@ -13,23 +13,26 @@
 //    coalesce. Cached IO ports (JOYP, DIV, TIMA, TMA, TAC, IF, LCDC, STAT, LY,
 //    LYC, WY, IE) live in registers; every path that touches those addresses
 //    (CPU access, OAM DMA source, env-0 latches) goes through the cache.
-//  * Fetch: ROM banks 0-1 and the 256-byte boot ROM are staged in shared
-//    memory; other banks are read through the read-only path.
-//  * Execute: a phased interpreter. A 256-entry decode table (shared memory)
-//    gives each opcode a family and a memory-read mode; one read site, one
-//    family switch over SM83's regular encoding (registers packed into two
-//    u32, indexed by bit-field extract; ALU and CB families branch-free), one
-//    write site. A divergent warp executes little distinct code.
-//  * Post-instruction work is split. The reference updates the timer, DIV,
-//    STAT mode bits, stat_prev, LY and the frame counter after every
-//    instruction. Here the common case keeps derived state lazy: STAT's low
-//    bits and stat_prev are functions of (LY, scanline cycle, LYC, LCD on);
-//    DIV/TIMA advance by an accumulated cycle count that is applied exactly
-//    (the reference's edge-stepping timer_tick, which is additive over time)
-//    only when an edge or reload is due or a timer port is touched. An
-//    instruction that halts, traps, writes LCDC/LY or an RTC register, or
-//    takes an interrupt, runs the reference's post-processing verbatim on
-//    materialised state (slow_post). Results are bit-identical.
+//  * Fetch: the ROM is pre-decoded on the host into one 32-bit word per byte
+//    (opcode, 16-bit immediate, family, memory-read mode). Banks 0-1 of it sit
+//    in shared memory, so fetch + decode is a single 4-byte shared load; other
+//    banks come through the read-only path. Code outside ROM (RAM, the boot
+//    ROM overlay, bank-crossing fetches) is decoded from bytes.
+//  * Execute: one read site, one switch over 30 families of SM83's regular
+//    encoding (registers packed into two u32, indexed by bit-field extract;
+//    ALU and CB families branch-free), one write site.
+//  * Post-instruction work is lazy. The reference updates timer, DIV, STAT
+//    mode bits, stat_prev, LY, RTC and the frame counter after every
+//    instruction. Here one counter `clk` accumulates cycles and is compared
+//    with `next_ev`, the cycles until the earliest event (timer edge/reload,
+//    scanline boundary, frame end, RTC second). Until then every one of those
+//    values is a function of the state at the last sync plus `clk`, so the
+//    common instruction tail is `clk += cyc; if (clk >= next_ev | ev) ...`.
+//    An instruction that crosses an event, halts, traps, or writes a port
+//    with timing side effects (LCDC, LY, LYC, IF, IE, timer, RTC) or enables
+//    interrupts sets `ev` and runs the reference's post-processing verbatim on
+//    materialised state (slow_post). The reference's timer_tick is additive
+//    over time, so lumping event-free cycles is exact.
 //  * HALT: runs of 4-cycle halted iterations that cannot change anything
 //    observable except counters (no line boundary, no timer reload, no frame
 //    end) are applied in one batch.
@@ -43,19 +46,18 @@
 namespace gbx {
 
 // ---------------------------------------------------------------------------
-// Decode table
+// Decode
 // ---------------------------------------------------------------------------
 enum Family : uint8_t {
-  FM_NOP, FM_LD16, FM_ST_A_IND, FM_LD_A_IND, FM_INC16, FM_DEC16, FM_INC8, FM_DEC8,
-  FM_INCDEC_HL, FM_LD8_IMM, FM_ST_HL_IMM, FM_ROTA, FM_ST_SP16, FM_ADDHL, FM_TRAP,
-  FM_JR, FM_JRCC, FM_DAA, FM_CPL, FM_SCF, FM_CCF, FM_LDRR, FM_LDR_HL, FM_STHL_R,
-  FM_HALT, FM_ALU_R, FM_ALU_V, FM_RET, FM_POP, FM_JP, FM_JPHL, FM_CALL, FM_PUSH,
-  FM_RST, FM_CB, FM_ST_A_IO, FM_LD_A_IO, FM_SPADD, FM_LDSPHL, FM_DI, FM_EI
+  FM_LDRR, FM_LD16, FM_ST_A, FM_LD_A, FM_INCDEC16, FM_INCDEC8, FM_INCDEC_HL, FM_LD8_IMM,
+  FM_ST_HL_IMM, FM_ROTA, FM_ST_SP16, FM_ADDHL, FM_TRAP, FM_JR, FM_DAA, FM_FLAGOP,
+  FM_LDR_HL, FM_STHL_R, FM_HALT, FM_ALU_R, FM_ALU_V, FM_RET, FM_POP, FM_JP,
+  FM_CALL, FM_PUSH, FM_RST, FM_CB, FM_SPADD, FM_IME
 };
 enum ReadMode : uint8_t { RD_NONE, RD_HL, RD_BC, RD_DE, RD_A16, RD_FF_N, RD_FF_C, RD_SP };
 
-// entry = family | read_mode << 8
-__host__ __device__ constexpr uint16_t decode_entry(int op) {
+// entry = family | read_mode << 5 (CB-prefixed (HL) forms are fixed up from the CB byte)
+__host__ __device__ constexpr uint8_t decode_entry(int op) {
   int x = op >> 6, y = (op >> 3) & 7, z = op & 7;
   if (op == 0xCB) return FM_CB;
   if (op == 0x10 || op == 0xD3 || op == 0xDB || op == 0xDD || op == 0xE3 || op == 0xE4 ||
@@ -63,56 +65,52 @@ __host__ __device__ constexpr uint16_t decode_entry(int op) {
     return FM_TRAP;
   if (x == 1) {
     if (op == 0x76) return FM_HALT;
-    if (z == 6) return FM_LDR_HL | (RD_HL << 8);
+    if (z == 6) return FM_LDR_HL | (RD_HL << 5);
     if (y == 6) return FM_STHL_R;
     return FM_LDRR;
   }
-  if (x == 2) return z == 6 ? (FM_ALU_V | (RD_HL << 8)) : FM_ALU_R;
+  if (x == 2) return z == 6 ? (FM_ALU_V | (RD_HL << 5)) : FM_ALU_R;
   if (x == 0) {
     switch (z) {
-      case 0: return op == 0x00 ? FM_NOP : op == 0x08 ? FM_ST_SP16 : op == 0x18 ? FM_JR : FM_JRCC;
+      case 0: return op == 0x00 ? FM_LDRR : op == 0x08 ? FM_ST_SP16 : FM_JR;
       case 1: return (y & 1) ? FM_ADDHL : FM_LD16;
       case 2:
-        if (y & 1) return FM_LD_A_IND | ((op == 0x0A ? RD_BC : op == 0x1A ? RD_DE : RD_HL) << 8);
-        return FM_ST_A_IND;
-      case 3: return (y & 1) ? FM_DEC16 : FM_INC16;
-      case 4: return y == 6 ? (FM_INCDEC_HL | (RD_HL << 8)) : FM_INC8;
-      case 5: return y == 6 ? (FM_INCDEC_HL | (RD_HL << 8)) : FM_DEC8;
+        if (y & 1) return FM_LD_A | ((op == 0x0A ? RD_BC : op == 0x1A ? RD_DE : RD_HL) << 5);
+        return FM_ST_A;
+      case 3: return FM_INCDEC16;
+      case 4: case 5: return y == 6 ? (FM_INCDEC_HL | (RD_HL << 5)) : FM_INCDEC8;
       case 6: return y == 6 ? FM_ST_HL_IMM : FM_LD8_IMM;
-      default:
-        switch (y) {
-          case 4: return FM_DAA;
-          case 5: return FM_CPL;
-          case 6: return FM_SCF;
-          case 7: return FM_CCF;
-          default: return FM_ROTA;
-        }
+      default: return y == 4 ? FM_DAA : y >= 5 ? FM_FLAGOP : FM_ROTA;
     }
   }
   switch (op) {  // x == 3
     case 0xC0: case 0xC8: case 0xD0: case 0xD8: case 0xC9: case 0xD9:
-      return FM_RET | (RD_SP << 8);
-    case 0xC1: case 0xD1: case 0xE1: case 0xF1: return FM_POP | (RD_SP << 8);
-    case 0xC2: case 0xCA: case 0xD2: case 0xDA: case 0xC3: return FM_JP;
-    case 0xE9: return FM_JPHL;
+      return FM_RET | (RD_SP << 5);
+    case 0xC1: case 0xD1: case 0xE1: case 0xF1: return FM_POP | (RD_SP << 5);
+    case 0xC2: case 0xCA: case 0xD2: case 0xDA: case 0xC3: case 0xE9: return FM_JP;
     case 0xC4: case 0xCC: case 0xD4: case 0xDC: case 0xCD: return FM_CALL;
     case 0xC5: case 0xD5: case 0xE5: case 0xF5: return FM_PUSH;
-    case 0xE0: case 0xE2: case 0xEA: return FM_ST_A_IO;
-    case 0xF0: return FM_LD_A_IO | (RD_FF_N << 8);
-    case 0xF2: return FM_LD_A_IO | (RD_FF_C << 8);
-    case 0xFA: return FM_LD_A_IO | (RD_A16 << 8);
-    case 0xE8: case 0xF8: return FM_SPADD;
-    case 0xF9: return FM_LDSPHL;
-    case 0xF3: return FM_DI;
-    case 0xFB: return FM_EI;
+    case 0xE0: case 0xE2: case 0xEA: return FM_ST_A;
+    case 0xF0: return FM_LD_A | (RD_FF_N << 5);
+    case 0xF2: return FM_LD_A | (RD_FF_C << 5);
+    case 0xFA: return FM_LD_A | (RD_A16 << 5);
+    case 0xE8: case 0xF8: case 0xF9: return FM_SPADD;
+    case 0xF3: case 0xFB: return FM_IME;
     default: break;
   }
   if (z == 6) return FM_ALU_V;  // ALU A,d8
   return FM_RST;                // z == 7
 }
 
+// 32-bit decoded instruction: opcode | imm16 << 8 | entry << 24
+__host__ __device__ constexpr uint32_t decode_word(int op, int b1, int b2) {
+  uint32_t e = decode_entry(op);
+  if (op == 0xCB && (b1 & 7) == 6) e |= RD_HL << 5;
+  return (uint32_t)op | ((uint32_t)b1 << 8) | ((uint32_t)b2 << 16) | (e << 24);
+}
+
 struct DecodeTable {
-  uint16_t e[256];
+  uint8_t e[256];
 };
 __host__ __device__ constexpr DecodeTable make_table() {
   DecodeTable t{};
@@ -121,52 +119,62 @@ __host__ __device__ constexpr DecodeTable make_table() {
 }
 __constant__ DecodeTable c_decode = make_table();
 
+// Host: pre-decode a ROM image (every byte offset as an instruction start).
+void predecode_rom(const uint8_t* rom, int n, uint32_t* out) {
+  for (int i = 0; i < n; i++) {
+    int b1 = i + 1 < n ? rom[i + 1] : 0, b2 = i + 2 < n ? rom[i + 2] : 0;
+    out[i] = decode_word(rom[i], b1, b2);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Per-thread emulator state
 // ---------------------------------------------------------------------------
 #define FLAGS(z, n, h, c) ((((z) ? 1 : 0) << 7) | (((n) ? 1 : 0) << 6) | (((h) ? 1 : 0) << 5) | (((c) ? 1 : 0) << 4))
 
 // events that send an instruction's post-processing down the exact path
-enum Event { EV_FIRST = 1, EV_HALT = 2, EV_TRAP = 4, EV_LCDC = 8, EV_PPU = 16, EV_RTC = 32 };
+enum Event { EV_FIRST = 1, EV_HALT = 2, EV_TRAP = 4, EV_LCDC = 8, EV_PPU = 16, EV_RTC = 32, EV_IRQ = 64,
+             EV_TIMER = 128 };
 
 template <int MBC>
 struct Emu {
   // addressing
-  uint8_t* mem;          // &st.mem[env]; byte a at mem[a * S]
+  uint8_t* mem;           // &st.mem[env]; byte a at mem[a * S]
   uint32_t S;
-  const uint8_t* rom_s;  // shared memory: rom[0 .. rom_s_bytes)
-  const uint8_t* boot_s; // shared memory: boot ROM
-  const uint8_t* rom_g;  // global ROM
-  int32_t* cart_state;   // &st.cart_state[env]
-  uint8_t* cart_ram;     // &st.cart_ram[env]
-  uint8_t* serial;       // &st.serial[env]
-  int32_t* i32;          // &st.i32[env]
-  uint8_t* u8s;          // &st.u8s[env]
-  uint8_t* latch;        // st.latch
+  const uint32_t* pre_s;  // shared memory: pre-decoded rom[0 .. pre_s_words)
+  const uint32_t* pre_g;  // global pre-decoded ROM
+  const uint8_t* boot_s;  // shared memory: boot ROM
+  const uint8_t* rom_g;   // global ROM bytes
+  int32_t* cart_state;    // &st.cart_state[env]
+  uint8_t* cart_ram;      // &st.cart_ram[env]
+  uint8_t* serial;        // &st.serial[env]
+  int32_t* i32;           // &st.i32[env]
+  uint8_t* u8s;           // &st.u8s[env]
+  uint8_t* latch;         // st.latch
   int rom_bank_count, rom_bank_mask, ram_bank_count;
-  int rom_s_bytes;
+  int pre_s_words;
   int is_env0;
   // CPU
   uint32_t bcde, hlxa;   // B C D E | H L - A, high byte first
   int f, pc, sp;
-  int ime, ime_delay, halted, ime_mask;
+  int ime, ime_delay, halted;
   int trap;
   // cached IO ports (values of mem[FFxx]); stat/div_b/prev_in/stat_prev are
   // exact only while lazy == 0
   int joyp, div_b, tima, tma, tac, iflag, lcdc, stat, ly_b, lyc, wy, ie;
   // timer
   int div, rl_pending, rl_delay, prev_in;
-  int t_acc, t_next;     // lazy: cycles not yet applied, cycles to the next edge/reload
   // PPU
   int scan, ly, wl, stat_prev;
-  int stat_hi, lcd_on;   // lazy: STAT bits 3-7, LCD on at the last refresh
   // cart
   int ram_en, bank_lo, bank_hi, ram_bank, bank_mode, bootrom, rtc_sel, rtc_latch;
   int bank0_off, bankN_off;   // ROM byte offset of a bank region; -1 when out of range
-  int rtc_sub, rtc_s, rtc_m, rtc_h, rtc_dl, rtc_dh, rtc_run;
+  int rtc_sub, rtc_s, rtc_m, rtc_h, rtc_dl, rtc_dh;
   // step
   int frames_done, release, action;
-  int ev, lazy, lcdc_before;
+  int cycle_frame, cyc_run, ninstr;
+  // lazy state
+  int lazy, ev, clk, next_ev, stat_hi, lcd_on, rtc_run, lcdc_before;
 
   // ---- registers -------------------------------------------------------
   __device__ __forceinline__ int A() const { return hlxa & 0xFF; }
@@ -221,33 +229,27 @@ struct Emu {
     bankN_off = bn < cnt ? bn * ROM_BANK - ROM_BANK : -1;
   }
 
-  __device__ __forceinline__ int rom_byte(int idx) const {
-    return idx < rom_s_bytes ? rom_s[idx] : __ldg(rom_g + idx);
-  }
   __device__ __forceinline__ int rom_read(int a) const {
     if (a < 0x100 && bootrom) return boot_s[a];
     int off = a < 0x4000 ? bank0_off : bankN_off;
     if (off < 0) return 0xFF;
-    return rom_byte(off + a);
+    return __ldg(rom_g + off + a);
   }
 
-  // STAT low bits / stat_prev as functions of the PPU position (lazy mode)
-  __device__ __forceinline__ int ppu_mode() const {
-    return ly >= SCREEN_H ? 1 : scan < 80 ? 2 : scan < 250 ? 3 : 0;
-  }
-  __device__ __forceinline__ int stat_now() const {
-    if (!lazy) return stat;
-    return stat_hi | ((ly == lyc) << 2) | (lcd_on ? ppu_mode() : 0);
+  // STAT low bits / stat_prev / DIV as functions of the state at the last
+  // sync plus clk (lazy mode)
+  __device__ __forceinline__ int ppu_mode_at(int sc) const {
+    return ly >= SCREEN_H ? 1 : sc < 80 ? 2 : sc < 250 ? 3 : 0;
   }
   __device__ __forceinline__ static int prev_bits(int mode, int coinc) {
     return (mode == 0) | ((mode == 1) << 1) | ((mode == 2) << 2) | (coinc << 3);
   }
-  __device__ __forceinline__ int stat_prev_now() const {
-    if (!lazy) return stat_prev;
-    return lcd_on ? prev_bits(ppu_mode(), ly == lyc) : 0;
+  __device__ __forceinline__ int stat_now() const {
+    if (!lazy) return stat;
+    return stat_hi | ((ly == lyc) << 2) | (lcd_on ? ppu_mode_at(scan + clk) : 0);
   }
   __device__ __forceinline__ int div_byte_now() const {
-    return lazy ? (((div + t_acc) >> 8) & 0xFF) : div_b;
+    return lazy ? (((div + clk) >> 8) & 0xFF) : div_b;
   }
 
   __device__ __forceinline__ int io_read(int a) const {
@@ -303,13 +305,15 @@ struct Emu {
     return cart_ram[(size_t)off * S];
   }
 
+  // read8 (:539-657); region = a >> 13: 4 VRAM and 6 WRAM first
   __device__ __forceinline__ int read8(int addr) const {
-    int a = addr & 0xFFFF;
-    if (a < 0x8000) return rom_read(a);
+    const int a = addr & 0xFFFF;
+    const int r = a >> 13;
+    if ((r | 2) == 6) return M(a);
+    if (r < 4) return rom_read(a);
+    if (r == 5) return cart_read(a);
     if (a >= 0xFF00) return io_read(a);
-    if (a >= 0xE000 && a < 0xFE00) a -= 0x2000;
-    if (a >= 0xA000 && a < 0xC000) return cart_read(a);
-    return M(a);
+    return M(a < 0xFE00 ? a - 0x2000 : a);
   }
 
   // ---- timer (cpu_step_builder.py:249-372) ------------------------------------
@@ -362,7 +366,7 @@ struct Emu {
     prev_in = timer_in(div, tac);
   }
   // cycles from now until timer_tick would do more than advance DIV
-  __device__ __forceinline__ void calc_t_next() {
+  __device__ __forceinline__ int timer_event() const {
     int t = INT_MAX;
     if (rl_pending) t = rl_delay;
     if (tac & 4) {
@@ -370,14 +374,7 @@ struct Emu {
       int e = period - (div & (period - 1));
       t = e < t ? e : t;
     }
-    t_next = t;
-  }
-  // apply the accumulated cycles exactly
-  __device__ void timer_sync() {
-    int c = t_acc;
-    t_acc = 0;
-    timer_tick(c);
-    calc_t_next();
+    return t;
   }
 
   // ---- MBC3 RTC (:375-419) ---------------------------------------------------
@@ -422,22 +419,6 @@ struct Emu {
     L[8 * SCREEN_H + line] = M(0xFF49);
   }
 
-  // one line boundary: window line, LY, STAT edge IRQ, VBlank, latch.
-  // keep = STAT bits 3-7; sp = stat_prev before the line (updated)
-  __device__ __forceinline__ void line_step(int l, int keep, int& sp) {
-    int prev = ly;
-    if (prev < SCREEN_H && (l & 0x20) && prev >= wy) wl++;
-    ly = ly + 1 == LINES_PER_FRAME ? 0 : ly + 1;
-    if (ly == 0) wl = 0;
-    ly_b = ly;
-    int mode = ly >= SCREEN_H ? 1 : 0;
-    int cur = prev_bits(mode, ly == lyc);
-    if ((keep >> 3) & cur & ~(sp & 0xF)) iflag |= 0x02;
-    sp = cur;
-    if (prev == 143 && ly == 144) iflag |= 0x01;
-    if (ly < SCREEN_H) latch0(ly);
-  }
-
   // the reference's advance block, exact (lazy == 0); returns the LCDC it read
   __device__ int ppu_advance(int cycles) {
     int l = lcdc;
@@ -451,52 +432,67 @@ struct Emu {
     int lines = total / CYCLES_PER_LINE;
     scan = total - lines * CYCLES_PER_LINE;
     if (lines == 0 && scan == 0) latch0(ly);
-    int sp = stat_prev;
     while (lines > 0) {
-      line_step(l, stat & 0xF8, sp);
+      int prev = ly;
+      if (prev < SCREEN_H && (l & 0x20) && prev >= wy) wl++;
+      ly = ly + 1 == LINES_PER_FRAME ? 0 : ly + 1;
+      if (ly == 0) wl = 0;
+      ly_b = ly;
+      // ppu_update_stat_irq: rising edge of an enabled condition sets IF bit 1
+      int keep = stat & 0xF8, c = ly == lyc, mode = ly >= SCREEN_H ? 1 : 0;
+      stat = keep | (c << 2) | mode;
+      int cur = prev_bits(mode, c);
+      if ((keep >> 3) & cur & ~(stat_prev & 0xF)) iflag |= 0x02;
+      stat_prev = cur;
+      if (prev == 143 && ly == 144) iflag |= 0x01;
+      if (ly < SCREEN_H) latch0(ly);
       lines--;
     }
-    int mode = ppu_mode();
+    int mode = ppu_mode_at(scan);
     int c = ly == lyc;
     stat = (stat & 0xF8) | (c << 2) | mode;
     stat_prev = prev_bits(mode, c);
     return l;
   }
 
-  // lazy advance (lazy == 1, no LCDC/LY write in this instruction)
-  __device__ __forceinline__ void ppu_lazy(int cycles) {
-    if (!lcd_on) return;
-    int total = scan + cycles;
-    if (total < CYCLES_PER_LINE) { scan = total; return; }
-    int sp = prev_bits(ppu_mode(), ly == lyc);  // stat_prev as of the last refresh
-    int lines = total / CYCLES_PER_LINE;
-    scan = total - lines * CYCLES_PER_LINE;
-    while (lines > 0) {
-      line_step(lcdc, stat_hi, sp);
-      lines--;
-    }
-  }
-
   // ---- lazy <-> exact --------------------------------------------------------
+  // Advance every lazily tracked counter by q event-free cycles.
+  __device__ void apply_quiet(int q) {
+    if (q <= 0) return;
+    timer_tick(q);  // no edge or reload inside q (q < next_ev)
+    if (lcd_on) scan += q;
+    if (MBC == MBC_MBC3) rtc_sub += q & rtc_run;
+    cycle_frame += q;
+    cyc_run += q;
+  }
+  // Turn derived values into stored ones (clk must be 0).
   __device__ void materialize() {
     if (!lazy) return;
-    stat = stat_now();
-    stat_prev = stat_prev_now();
+    stat = stat_hi | ((ly == lyc) << 2) | (lcd_on ? ppu_mode_at(scan) : 0);
+    stat_prev = lcd_on ? prev_bits(ppu_mode_at(scan), ly == lyc) : 0;
+    div_b = (div >> 8) & 0xFF;
+    prev_in = timer_in(div, tac);
     lazy = 0;
-    int c = t_acc;
-    t_acc = 0;
-    timer_tick(c);  // no edge/reload is due (t_acc < t_next)
-    if (c == 0) { div_b = (div >> 8) & 0xFF; prev_in = timer_in(div, tac); }
   }
-  // after an exact post: derived values agree with the state again
+  // Bring everything up to date (apply clk, materialise).
+  __device__ void sync_all() {
+    if (!lazy) return;
+    apply_quiet(clk);
+    clk = 0;
+    materialize();
+  }
+  // After exact processing: derived values agree with the state again.
   __device__ void delazify() {
     lazy = 1;
     stat_hi = stat & 0xF8;
     lcd_on = (lcdc & 0x80) != 0;
-    t_acc = 0;
-    calc_t_next();
-    ime_mask = ime ? 0x1F : 0;
-    rtc_run = (rtc_dh & 0x40) ? 0 : -1;
+    rtc_run = (MBC == MBC_MBC3 && !(rtc_dh & 0x40) && rtc_sub >= 0) ? -1 : 0;
+    int t = timer_event();
+    if (lcd_on) { int p = CYCLES_PER_LINE - scan; t = p < t ? p : t; }
+    { int fr = CYCLES_PER_FRAME - cycle_frame; t = fr < t ? fr : t; }
+    if (MBC == MBC_MBC3 && rtc_run) { int r = RTC_CPS - rtc_sub; t = r < t ? r : t; }
+    next_ev = t;
+    clk = 0;
     ev = 0;
   }
 
@@ -517,88 +513,91 @@ struct Emu {
     return v | 0xC0;
   }
 
-  __device__ void write8(int addr, int val) {
-    int a = addr & 0xFFFF;
-    if (a >= 0xE000 && a < 0xFE00) a -= 0x2000;
-    int v8 = val & 0xFF;
-    if (a >= 0xFF00) {
-      switch (a & 0xFF) {
-        case 0x00: {
-          int sel = v8 & 0x30;
-          u8s[(size_t)F_JOYP_SELECT * S] = (uint8_t)sel;
-          joyp = joyp_value(sel);
-          return;
-        }
-        case 0x0F: iflag = v8 & 0x1F; return;
-        case 0x02:
-          if ((val & 0x80) && (val & 0x01)) {
-            int idx = i32[(size_t)F_SERIAL_LEN * S];
-            if (idx < SERIAL_MAX) {
-              serial[(size_t)idx * S] = M(0xFF01);
-              i32[(size_t)F_SERIAL_LEN * S] = idx + 1;
-            } else {
-              u8s[(size_t)F_SERIAL_OVERFLOW * S] = 1;
-            }
-            M(0xFF02) = (uint8_t)(val & 0x7F);
-            iflag |= 0x08;
-          } else {
-            M(0xFF02) = (uint8_t)v8;
-          }
-          return;
-        case 0x50:
-          if (val != 0) bootrom = 0;
-          return;
-        case 0x04: case 0x05: case 0x06: case 0x07: {
-          if (lazy) timer_sync();
-          int reg = a & 0xFF;
-          if (reg == 0x05) { tima = v8; }
-          else if (reg == 0x06) { tma = v8; }
-          else if (reg == 0x04) {
-            int pre = timer_in(div & 0xFFFF, tac);
-            div_b = 0;
-            div = 0;
-            int post = timer_in(0, tac);
-            prev_in = post;
-            if (pre && !post) tima_inc();
-          } else {
-            int pre = timer_in(div & 0xFFFF, tac);
-            int tn = val & 7;
-            tac = tn;
-            int post = timer_in(div & 0xFFFF, tn);
-            prev_in = post;
-            if (pre && !post) tima_inc();
-          }
-          if (lazy) calc_t_next();
-          return;
-        }
-        case 0x46: {
-          M(0xFF46) = (uint8_t)v8;
-          int src = (val & 0xFF) << 8;
-          if (src < 0xFF00) {
-            for (int o = 0; o < 160; o++) M(0xFE00 + o) = M((src + o) & 0xFFFF);
-          } else {
-            for (int o = 0; o < 160; o++) M(0xFE00 + o) = (uint8_t)raw_read(src + o);
-          }
-          return;
-        }
-        case 0xFF: ie = v8 & 0x1F; return;
-        case 0x40:
-          if (!(ev & EV_LCDC)) lcdc_before = lcdc;
-          lcdc = v8;
-          ev |= EV_LCDC;
-          return;
-        case 0x41: stat = v8; stat_hi = v8 & 0xF8; return;
-        case 0x44: ly_b = v8; ev |= EV_PPU; return;
-        case 0x45:
-          // stat_prev of the last refresh was computed with the old LYC
-          if (lazy) materialize();
-          lyc = v8;
-          ev |= EV_PPU;
-          return;
-        case 0x4A: wy = v8; return;
-        default: M(a) = (uint8_t)v8; return;
+  __device__ void write_io(int a, int val) {
+    const int v8 = val & 0xFF;
+    switch (a & 0xFF) {
+      case 0x00: {
+        int sel = v8 & 0x30;
+        u8s[(size_t)F_JOYP_SELECT * S] = (uint8_t)sel;
+        joyp = joyp_value(sel);
+        return;
       }
+      case 0x0F: iflag = v8 & 0x1F; ev |= EV_IRQ; return;
+      case 0x02:
+        if ((val & 0x80) && (val & 0x01)) {
+          int idx = i32[(size_t)F_SERIAL_LEN * S];
+          if (idx < SERIAL_MAX) {
+            serial[(size_t)idx * S] = M(0xFF01);
+            i32[(size_t)F_SERIAL_LEN * S] = idx + 1;
+          } else {
+            u8s[(size_t)F_SERIAL_OVERFLOW * S] = 1;
+          }
+          M(0xFF02) = (uint8_t)(val & 0x7F);
+          iflag |= 0x08;
+          ev |= EV_IRQ;
+        } else {
+          M(0xFF02) = (uint8_t)v8;
+        }
+        return;
+      case 0x50:
+        if (val != 0) bootrom = 0;
+        return;
+      case 0x04: case 0x05: case 0x06: case 0x07: {
+        sync_all();
+        int reg = a & 0xFF;
+        if (reg == 0x05) { tima = v8; }
+        else if (reg == 0x06) { tma = v8; }
+        else if (reg == 0x04) {
+          int pre = timer_in(div & 0xFFFF, tac);
+          div_b = 0;
+          div = 0;
+          int post = timer_in(0, tac);
+          prev_in = post;
+          if (pre && !post) tima_inc();
+        } else {
+          int pre = timer_in(div & 0xFFFF, tac);
+          int tn = val & 7;
+          tac = tn;
+          int post = timer_in(div & 0xFFFF, tn);
+          prev_in = post;
+          if (pre && !post) tima_inc();
+        }
+        ev |= EV_TIMER;
+        return;
+      }
+      case 0x46: {
+        M(0xFF46) = (uint8_t)v8;
+        int src = (val & 0xFF) << 8;
+        if (src < 0xFF00) {
+          for (int o = 0; o < 160; o++) M(0xFE00 + o) = M((src + o) & 0xFFFF);
+        } else {
+          for (int o = 0; o < 160; o++) M(0xFE00 + o) = (uint8_t)raw_read(src + o);
+        }
+        return;
+      }
+      case 0xFF: ie = v8 & 0x1F; ev |= EV_IRQ; return;
+      case 0x40:
+        if (!(ev & EV_LCDC)) lcdc_before = lcdc;
+        lcdc = v8;
+        ev |= EV_LCDC;
+        return;
+      case 0x41: stat = v8; stat_hi = v8 & 0xF8; return;
+      case 0x44: ly_b = v8; ev |= EV_PPU; return;
+      case 0x45:
+        // stat_prev of the last refresh was computed with the old LYC
+        sync_all();
+        lyc = v8;
+        ev |= EV_PPU;
+        return;
+      case 0x4A: wy = v8; return;
+      default: M(a) = (uint8_t)v8; return;
     }
+  }
+
+  __device__ void write8_slow(int a, int val) {
+    const int v8 = val & 0xFF;
+    if (a >= 0xFF00) { write_io(a, val); return; }
+    if (a >= 0xE000 && a < 0xFE00) { M(a - 0x2000) = (uint8_t)v8; return; }
     if (a >= 0xA000 && a < 0xC000) {
       if (ram_bank_count <= 0 || ram_en == 0) return;
       if (MBC == MBC_MBC3) {
@@ -640,7 +639,13 @@ struct Emu {
       }
       return;
     }
-    M(a) = (uint8_t)v8;
+    M(a) = (uint8_t)v8;  // FE00-FEFF
+  }
+
+  __device__ __forceinline__ void write8(int addr, int val) {
+    const int a = addr & 0xFFFF;
+    if (((a >> 13) | 2) == 6) { M(a) = (uint8_t)val; return; }  // VRAM, WRAM
+    write8_slow(a, val);
   }
 
   // ---- ALU (alu.py), branch-free over the 8 kinds ----------------------------
@@ -663,142 +668,128 @@ struct Emu {
     int bit = (cc & 2) ? ((f >> 4) & 1) : ((f >> 7) & 1);
     return (cc & 1) ? bit : !bit;
   }
+
+  // interrupt service (:1502-1604): IME off, IF bit cleared, PC pushed
+  __device__ void service(int pending) {
+    int bit = pending & (-pending);  // lowest set bit = highest priority
+    int vector = 0x40 + 8 * (31 - __clz(bit));
+    ime = 0;
+    iflag &= 0xFF ^ bit;
+    int ret = pc;
+    sp = (sp - 1) & 0xFFFF;
+    write8(sp, ret >> 8);
+    sp = (sp - 1) & 0xFFFF;
+    write8(sp, ret & 0xFF);
+    pc = vector;
+  }
+
+  // ---- exact per-instruction tail (:1375-1758) ---------------------------------
+  // Runs after an instruction of `cyc` cycles whose tail could not stay lazy.
+  __device__ void slow_post(int cyc, int opcode, int pc_before, int frames_to_run) {
+    const int lcdc_prev = ((ev & EV_LCDC) ? lcdc_before : lcdc) & 0x80;
+    if (lazy) {
+      apply_quiet(clk - cyc);  // the event-free cycles of earlier instructions
+      clk = 0;
+      materialize();
+    }
+    timer_tick(cyc);
+    if (ime_delay) { ime = 1; ime_delay = 0; }
+    int lcdc_now = ppu_advance(cyc);
+    const int pending = ie & iflag & 0x1F;
+    int svc = 0;
+    if (pending) {
+      if (halted) halted = 0;
+      if (ime) {
+        service(pending);
+        svc = 20;
+        timer_tick(20);
+        lcdc_now = ppu_advance(20);
+      }
+    }
+    const int total = cyc + svc;
+    rtc_tick(total);
+    cyc_run += total;
+    cycle_frame += total;
+    if (lcdc_prev && !(lcdc_now & 0x80)) {
+      int tail = total;
+      if (opcode == 0xE0 && (read8((pc_before + 1) & 0xFFFF) & 0xFF) == 0x40 && cyc >= 4) tail = total - 4;
+      cycle_frame = tail;
+      frames_done++;
+    } else if (!lcdc_prev && (lcdc_now & 0x80)) {
+      scan = 0; ly = 0; wl = 0; ly_b = 0;
+      stat = (stat & 0xF8) | ((lyc == 0) << 2) | 2;
+      stat_prev = (1 << 2) | ((lyc == 0) << 3);
+      cycle_frame = 0;
+      frames_done++;
+    } else {
+      while (cycle_frame >= CYCLES_PER_FRAME) {
+        cycle_frame -= CYCLES_PER_FRAME;
+        frames_done++;
+        if (frames_done >= frames_to_run) break;
+      }
+    }
+    delazify();
+  }
+
+  // One halted iteration (:976-1300), or a batch of them that no event can
+  // interrupt. Exact state in and out.
+  __device__ void halted_step(int frames_to_run) {
+    const int lcdc_prev = lcdc & 0x80;
+    int k = 1;
+    if ((ie & iflag & 0x1F) == 0 && cycle_frame < CYCLES_PER_FRAME) {
+      int kmax = (CYCLES_PER_FRAME - cycle_frame + 3) >> 2;  // iteration that ends the frame
+      if (lcdc & 0x80) {
+        int kl = (CYCLES_PER_LINE - scan + 3) >> 2;          // iteration that crosses a line
+        kmax = kl < kmax ? kl : kmax;
+      }
+      if ((tac & 4) || rl_pending) {
+        int t;
+        if (rl_pending) {
+          t = rl_delay;
+        } else {
+          int period = 1 << (div_bit(tac) + 1);
+          t = period - (div & (period - 1)) + (0xFF - tima) * period + 4;
+        }
+        int kt = t <= 0 ? 1 : (t + 3) >> 2;                  // iteration of the next TIMA reload
+        kmax = kt < kmax ? kt : kmax;
+      }
+      k = kmax - 1;
+      if (k < 1) k = 1;
+    }
+    const int cycles = 4 * k;
+    timer_tick(cycles);
+    int lcdc_now = ppu_advance(cycles);
+    const int pending = ie & iflag & 0x1F;
+    int svc = 0;
+    if (pending) {
+      halted = 0;
+      if (ime) {
+        service(pending);
+        svc = 20;
+        timer_tick(20);
+        lcdc_now = ppu_advance(20);
+      } else {
+        pc = (pc + 1) & 0xFFFF;  // :1181-1183
+      }
+    }
+    const int total = cycles + svc;
+    rtc_tick(total);
+    cyc_run += total;
+    cycle_frame += total;
+    if (lcdc_prev && !(lcdc_now & 0x80)) {
+      cycle_frame = 0;
+      frames_done++;
+      return;
+    }
+    while (cycle_frame >= CYCLES_PER_FRAME) {
+      cycle_frame -= CYCLES_PER_FRAME;
+      frames_done++;
+      if (frames_done >= frames_to_run) break;
+    }
+  }
 };
 
 __device__ __forceinline__ int sign8(int v) { return v >= 128 ? v - 256 : v; }
-
-// ---------------------------------------------------------------------------
-// Post-processing, exact (the reference's per-instruction tail)
-// ---------------------------------------------------------------------------
-// stage 0: nothing applied yet for this instruction's `cyc` cycles.
-// stage 1: timer and PPU already advanced lazily by `cyc` (the fast path found
-//          a pending interrupt).
-template <int MBC>
-__device__ void slow_post(Emu<MBC>& s, int cyc, int opcode, int pc_before, int stage, int frames_to_run,
-                          int& cycle_frame, long long& cyc_total) {
-  const int lcdc_prev = ((s.ev & EV_LCDC) ? s.lcdc_before : s.lcdc) & 0x80;
-  s.materialize();
-  int lcdc_now;
-  if (stage == 0) {
-    s.timer_tick(cyc);
-    if (s.ime_delay) { s.ime = 1; s.ime_delay = 0; }
-    lcdc_now = s.ppu_advance(cyc);
-  } else {
-    lcdc_now = s.lcdc;
-  }
-  const int pending = s.ie & s.iflag & 0x1F;
-  int svc = 0;
-  if (pending) {
-    if (s.halted) s.halted = 0;
-    if (s.ime) {
-      int bit = pending & (-pending);  // lowest set bit = highest priority
-      int vector = 0x40 + 8 * (31 - __clz(bit));
-      s.ime = 0;
-      s.iflag &= 0xFF ^ bit;
-      int ret = s.pc;
-      s.sp = (s.sp - 1) & 0xFFFF;
-      s.write8(s.sp, ret >> 8);
-      s.sp = (s.sp - 1) & 0xFFFF;
-      s.write8(s.sp, ret & 0xFF);
-      s.pc = vector;
-      svc = 20;
-      s.timer_tick(20);
-      lcdc_now = s.ppu_advance(20);
-    }
-  }
-  const int total = cyc + svc;
-  s.rtc_tick(total);
-  cyc_total += total;
-  cycle_frame += total;
-  // frame accounting (:1706-1758)
-  if (lcdc_prev && !(lcdc_now & 0x80)) {
-    int tail = total;
-    if (opcode == 0xE0 && (s.read8((pc_before + 1) & 0xFFFF) & 0xFF) == 0x40 && cyc >= 4) tail = total - 4;
-    cycle_frame = tail;
-    s.frames_done++;
-  } else if (!lcdc_prev && (lcdc_now & 0x80)) {
-    s.scan = 0; s.ly = 0; s.wl = 0; s.ly_b = 0;
-    s.stat = (s.stat & 0xF8) | ((s.lyc == 0) << 2) | 2;
-    s.stat_prev = (1 << 2) | ((s.lyc == 0) << 3);
-    cycle_frame = 0;
-    s.frames_done++;
-  } else {
-    while (cycle_frame >= CYCLES_PER_FRAME) {
-      cycle_frame -= CYCLES_PER_FRAME;
-      s.frames_done++;
-      if (s.frames_done >= frames_to_run) break;
-    }
-  }
-  s.delazify();
-}
-
-// One halted iteration (:976-1300), or a batch of them that no event can
-// interrupt. Exact state in and out.
-template <int MBC>
-__device__ void halted_step(Emu<MBC>& s, int frames_to_run, int& cycle_frame, long long& cyc_total) {
-  const int lcdc_prev = s.lcdc & 0x80;
-  int k = 1;
-  const int pending0 = s.ie & s.iflag & 0x1F;
-  if (pending0 == 0 && cycle_frame < CYCLES_PER_FRAME) {
-    int kmax = (CYCLES_PER_FRAME - cycle_frame + 3) >> 2;  // iteration that ends the frame
-    if (s.lcdc & 0x80) {
-      int kl = (CYCLES_PER_LINE - s.scan + 3) >> 2;        // iteration that crosses a line
-      kmax = kl < kmax ? kl : kmax;
-    }
-    if ((s.tac & 4) || s.rl_pending) {
-      int t;
-      if (s.rl_pending) {
-        t = s.rl_delay;
-      } else {
-        int period = 1 << (Emu<MBC>::div_bit(s.tac) + 1);
-        t = period - (s.div & (period - 1)) + (0xFF - s.tima) * period + 4;
-      }
-      int kt = t <= 0 ? 1 : (t + 3) >> 2;                  // iteration of the next TIMA reload
-      kmax = kt < kmax ? kt : kmax;
-    }
-    k = kmax - 1;
-    if (k < 1) k = 1;
-  }
-  const int cycles = 4 * k;
-  s.timer_tick(cycles);
-  int lcdc_now = s.ppu_advance(cycles);
-  const int pending = s.ie & s.iflag & 0x1F;
-  int svc = 0;
-  if (pending) {
-    s.halted = 0;
-    if (s.ime) {
-      int bit = pending & (-pending);
-      int vector = 0x40 + 8 * (31 - __clz(bit));
-      s.ime = 0;
-      s.iflag &= 0xFF ^ bit;
-      int ret = s.pc;
-      s.sp = (s.sp - 1) & 0xFFFF;
-      s.write8(s.sp, ret >> 8);
-      s.sp = (s.sp - 1) & 0xFFFF;
-      s.write8(s.sp, ret & 0xFF);
-      s.pc = vector;
-      svc = 20;
-      s.timer_tick(20);
-      lcdc_now = s.ppu_advance(20);
-    } else {
-      s.pc = (s.pc + 1) & 0xFFFF;  // :1181-1183
-    }
-  }
-  const int total = cycles + svc;
-  s.rtc_tick(total);
-  cyc_total += total;
-  cycle_frame += total;
-  if (lcdc_prev && !(lcdc_now & 0x80)) {
-    cycle_frame = 0;
-    s.frames_done++;
-    return;
-  }
-  while (cycle_frame >= CYCLES_PER_FRAME) {
-    cycle_frame -= CYCLES_PER_FRAME;
-    s.frames_done++;
-    if (s.frames_done >= frames_to_run) break;
-  }
-}
 
 // ---------------------------------------------------------------------------
 // The kernel
@@ -806,20 +797,19 @@ __device__ void halted_step(Emu<MBC>& s, int frames_to_run, int& cycle_frame, lo
 // K = envs per warp: lane l < K of global warp w runs env w*K + l. Small K
 // spreads few envs over many warps (no divergence, more latency hiding);
 // K = 32 packs a full warp (shared issue slots when envs run in lockstep).
-// REGCAP = 1 caps registers so 4 blocks of 256 threads fit per SM.
-template <int MBC, int REGCAP>
-__global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
-    gb_step_kernel(DevState st, const int32_t* __restrict__ actions, int frames_to_run, int release_after_frames,
-                   int stage, int K) {
+// MAXT = largest block size the launch may use (caps registers at 64K/MAXT).
+template <int MBC, int MAXT>
+__global__ void __launch_bounds__(MAXT, 1)
+    gb_step_kernel(DevState st, const uint32_t* __restrict__ pre_g, const int32_t* __restrict__ actions,
+                   int frames_to_run, int release_after_frames, int stage, int K, int pre_s_words) {
   extern __shared__ __align__(16) uint8_t smem[];
-  uint16_t* dec_s = reinterpret_cast<uint16_t*>(smem);
-  uint8_t* boot_s = smem + 512;
-  uint8_t* rom_s = smem + 768;
-  const int rom_s_bytes = st.rom_bytes < ROM_SMEM_MAX ? st.rom_bytes : ROM_SMEM_MAX;
+  uint32_t* pre_s = reinterpret_cast<uint32_t*>(smem);
+  uint8_t* boot_s = smem + (size_t)pre_s_words * 4;
+  uint8_t* dec_s = boot_s + 256;
   {
-    const uint4* src = reinterpret_cast<const uint4*>(st.rom);
-    uint4* dst = reinterpret_cast<uint4*>(rom_s);
-    for (int k = threadIdx.x; k < rom_s_bytes / 16; k += blockDim.x) dst[k] = __ldg(src + k);
+    const uint4* src = reinterpret_cast<const uint4*>(pre_g);
+    uint4* dst = reinterpret_cast<uint4*>(pre_s);
+    for (int k = threadIdx.x; k < pre_s_words / 4; k += blockDim.x) dst[k] = __ldg(src + k);
     for (int k = threadIdx.x; k < 256; k += blockDim.x) {
       boot_s[k] = st.boot[k];
       dec_s[k] = c_decode.e[k];
@@ -836,7 +826,8 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
   Emu<MBC> s;
   s.mem = st.mem + env;
   s.S = st.S;
-  s.rom_s = rom_s;
+  s.pre_s = pre_s;
+  s.pre_g = pre_g;
   s.boot_s = boot_s;
   s.rom_g = st.rom;
   s.cart_state = st.cart_state + env;
@@ -848,7 +839,7 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
   s.rom_bank_count = st.rom_bank_count;
   s.rom_bank_mask = st.rom_bank_mask;
   s.ram_bank_count = st.ram_bank_count;
-  s.rom_s_bytes = rom_s_bytes;
+  s.pre_s_words = pre_s_words;
   s.is_env0 = env == 0;
 
   const int32_t* I = st.i32 + env;
@@ -859,7 +850,7 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
            ((uint32_t)(ld(F_D) & 0xFF) << 8) | (uint32_t)(ld(F_E) & 0xFF);
   s.hlxa = ((uint32_t)(ld(F_H) & 0xFF) << 24) | ((uint32_t)(ld(F_L) & 0xFF) << 16) | (uint32_t)(ld(F_A) & 0xFF);
   s.f = ld(F_F) & 0xF0;
-  int cycle_frame = ld(F_CYCLE_IN_FRAME);
+  s.cycle_frame = ld(F_CYCLE_IN_FRAME);
   s.trap = ld(F_TRAP_FLAG);
   s.ime = ld(F_IME);
   s.ime_delay = ld(F_IME_DELAY);
@@ -872,8 +863,6 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
   s.ly = ld(F_PPU_LY);
   s.wl = ld(F_PPU_WINDOW_LINE);
   s.stat_prev = st.u8s[(size_t)F_STAT_PREV * S + env];
-  long long instr = st.i64[(size_t)F_INSTR_COUNT * S + env];
-  long long cyc_total = st.i64[(size_t)F_CYCLE_COUNT * S + env];
 
   s.joyp = s.M(0xFF00); s.div_b = s.M(0xFF04); s.tima = s.M(0xFF05); s.tma = s.M(0xFF06);
   s.tac = s.M(0xFF07); s.iflag = s.M(0xFF0F); s.lcdc = s.M(0xFF40); s.stat = s.M(0xFF41);
@@ -900,54 +889,45 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
   s.action = actions[env];
   s.release = release_after_frames;
   s.frames_done = 0;
-  // derived state is exact until the first exact post-processing
+  s.cyc_run = 0;
+  s.ninstr = 0;
+  // state is exact (lazy == 0) until the first exact tail has run
   s.lazy = 0;
   s.ev = EV_FIRST;
-  s.t_acc = 0;
-  s.t_next = INT_MAX;
+  s.clk = 0;
+  s.next_ev = INT_MAX;
   s.stat_hi = s.stat & 0xF8;
   s.lcd_on = 0;
-  s.ime_mask = 0;
   s.rtc_run = 0;
   s.lcdc_before = s.lcdc;
 
-  const uint16_t* dec = dec_s;
-
-  while (s.frames_done < frames_to_run) {
-    if (s.trap) break;
-    if (s.halted) {
-      s.materialize();
-      const int first = s.ev & EV_FIRST;
-      halted_step(s, frames_to_run, cycle_frame, cyc_total);
-      s.delazify();
-      s.ev = first;
-      continue;
-    }
-    // ---- fetch ----
-    const int pc_before = s.pc;
-    int opcode, imm8, imm16;
+  bool run = s.frames_done < frames_to_run && !s.trap;
+  // a halted start runs the halted loop first
+  if (run && s.halted) {
+    while (s.halted && s.frames_done < frames_to_run) s.halted_step(frames_to_run);
+    run = s.frames_done < frames_to_run;
+  }
+  while (run) {
+    // ---- fetch + decode ----
+    const int pc = s.pc;
+    uint32_t w;
     {
-      const int pc = s.pc;
       const int off = (pc & 0x4000) ? s.bankN_off : s.bank0_off;
-      // fast path: three bytes inside one ROM bank region, boot ROM not mapped there
       if (pc < 0x8000 && (pc & 0x3FFF) < 0x3FFE && off >= 0 && (pc >= 0x100 || !s.bootrom)) {
         const int idx = off + pc;
-        if (idx + 2 < s.rom_s_bytes) {
-          opcode = s.rom_s[idx]; imm8 = s.rom_s[idx + 1]; imm16 = imm8 | (s.rom_s[idx + 2] << 8);
-        } else {
-          opcode = __ldg(s.rom_g + idx); imm8 = __ldg(s.rom_g + idx + 1);
-          imm16 = imm8 | (__ldg(s.rom_g + idx + 2) << 8);
-        }
+        w = idx < s.pre_s_words ? s.pre_s[idx] : __ldg(s.pre_g + idx);
       } else {
-        opcode = s.read8(pc);
-        imm8 = s.read8(pc + 1);
-        imm16 = imm8 | (s.read8(pc + 2) << 8);
+        const int op = s.read8(pc), b1 = s.read8(pc + 1), b2 = s.read8(pc + 2);
+        uint32_t e = dec_s[op];
+        if (op == 0xCB && (b1 & 7) == 6) e |= RD_HL << 5;
+        w = (uint32_t)op | ((uint32_t)b1 << 8) | ((uint32_t)b2 << 16) | (e << 24);
       }
     }
-    const int e = dec[opcode];
-    const int fam = e & 0xFF;
-    int rmode = e >> 8;
-    if (fam == FM_CB && (imm8 & 7) == 6) rmode = RD_HL;
+    const int opcode = w & 0xFF;
+    const int imm8 = (w >> 8) & 0xFF;
+    const int imm16 = (w >> 8) & 0xFFFF;
+    const int fam = (w >> 24) & 31;
+    const int rmode = w >> 29;
     // ---- memory reads ----
     int v1 = 0, v2 = 0;
     if (rmode != RD_NONE) {
@@ -965,50 +945,56 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
       if (rmode == RD_SP) v2 = s.read8((ra + 1) & 0xFFFF);
     }
     // ---- execute ----
-    int pc = s.pc;
+    int npc = pc + 1;
     int cyc = 4;
     int nw = 0, wa0 = 0, wv0 = 0, wa1 = 0, wv1 = 0;
     const int y = (opcode >> 3) & 7, z = opcode & 7;
     switch (fam) {
-      case FM_NOP: pc += 1; break;
-      case FM_LD16: s.setp((opcode >> 4) & 3, imm16); pc += 3; cyc = 12; break;
-      case FM_ST_A_IND: {
-        int p = (opcode >> 4) & 3;  // 0 BC, 1 DE, 2 HL+, 3 HL-
-        int ad = p == 0 ? s.BC() : p == 1 ? s.DE() : s.HL();
-        nw = 1; wa0 = ad; wv0 = s.A();
-        if (p >= 2) s.setHL(p == 2 ? ad + 1 : ad - 1);
-        pc += 1; cyc = 8; break;
-      }
-      case FM_LD_A_IND: {
-        int p = (opcode >> 4) & 3;
+      case FM_LDRR: s.setr(y, s.getr(z)); break;  // includes NOP (LD B,B form)
+      case FM_LD16: s.setp((opcode >> 4) & 3, imm16); npc = pc + 3; cyc = 12; break;
+      case FM_ST_A:
+        nw = 1; wv0 = s.A();
+        if (opcode < 0x40) {
+          const int p = (opcode >> 4) & 3;  // 0 BC, 1 DE, 2 HL+, 3 HL-
+          const int ad = p == 0 ? s.BC() : p == 1 ? s.DE() : s.HL();
+          wa0 = ad;
+          if (p >= 2) s.setHL(p == 2 ? ad + 1 : ad - 1);
+          cyc = 8;
+        } else if (opcode == 0xE0) { wa0 = 0xFF00 | imm8; npc = pc + 2; cyc = 12; }
+        else if (opcode == 0xE2) { wa0 = 0xFF00 | s.C_(); cyc = 8; }
+        else { wa0 = imm16; npc = pc + 3; cyc = 16; }
+        break;
+      case FM_LD_A:
         s.setA(v1);
-        if (p >= 2) { int hl = s.HL(); s.setHL(p == 2 ? hl + 1 : hl - 1); }
-        pc += 1; cyc = 8; break;
+        if (opcode < 0x40) {
+          const int p = (opcode >> 4) & 3;
+          if (p >= 2) { const int hl = s.HL(); s.setHL(p == 2 ? hl + 1 : hl - 1); }
+          cyc = 8;
+        } else if (opcode == 0xF0) { npc = pc + 2; cyc = 12; }
+        else if (opcode == 0xF2) { cyc = 8; }
+        else { npc = pc + 3; cyc = 16; }
+        break;
+      case FM_INCDEC16: {
+        const int p = (opcode >> 4) & 3;
+        s.setp(p, s.getp(p) + ((opcode & 8) ? -1 : 1));
+        cyc = 8; break;
       }
-      case FM_INC16: { int p = (opcode >> 4) & 3; s.setp(p, s.getp(p) + 1); pc += 1; cyc = 8; break; }
-      case FM_DEC16: { int p = (opcode >> 4) & 3; s.setp(p, s.getp(p) - 1); pc += 1; cyc = 8; break; }
-      case FM_INC8: {
-        int old = s.getr(y), v = (old + 1) & 0xFF;
+      case FM_INCDEC8: {
+        const int dec1 = z & 1;
+        const int old = s.getr(y), v = (dec1 ? old - 1 : old + 1) & 0xFF;
         s.setr(y, v);
-        s.f = FLAGS(v == 0, 0, (old & 0xF) == 0xF, (s.f >> 4) & 1);
-        pc += 1; break;
-      }
-      case FM_DEC8: {
-        int old = s.getr(y), v = (old - 1) & 0xFF;
-        s.setr(y, v);
-        s.f = FLAGS(v == 0, 1, (old & 0xF) == 0, (s.f >> 4) & 1);
-        pc += 1; break;
+        s.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (s.f >> 4) & 1);
+        break;
       }
       case FM_INCDEC_HL: {
-        const int old = v1, dec1 = z == 5;
+        const int old = v1, dec1 = z & 1;
         const int v = (dec1 ? old - 1 : old + 1) & 0xFF;
-        const int h = dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF;
-        s.f = FLAGS(v == 0, dec1, h, (s.f >> 4) & 1);
+        s.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (s.f >> 4) & 1);
         nw = 1; wa0 = s.HL(); wv0 = v;
-        pc += 1; cyc = 12; break;
+        cyc = 12; break;
       }
-      case FM_LD8_IMM: s.setr(y, imm8); pc += 2; cyc = 8; break;
-      case FM_ST_HL_IMM: nw = 1; wa0 = s.HL(); wv0 = imm8; pc += 2; cyc = 12; break;
+      case FM_LD8_IMM: s.setr(y, imm8); npc = pc + 2; cyc = 8; break;
+      case FM_ST_HL_IMM: nw = 1; wa0 = s.HL(); wv0 = imm8; npc = pc + 2; cyc = 12; break;
       case FM_ROTA: {
         const int a = s.A(), oc = (s.f >> 4) & 1;
         const int right = y & 1, thru = y >> 1;
@@ -1016,22 +1002,20 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
         const int in = thru ? oc : c;
         const int r = right ? ((a >> 1) | (in << 7)) : (((a << 1) & 0xFF) | in);
         s.setA(r); s.f = FLAGS(0, 0, 0, c);
-        pc += 1; break;
+        break;
       }
       case FM_ST_SP16:
         nw = 2; wa0 = imm16; wv0 = s.sp & 0xFF; wa1 = (imm16 + 1) & 0xFFFF; wv1 = (s.sp >> 8) & 0xFF;
-        pc += 3; cyc = 20; break;
+        npc = pc + 3; cyc = 20; break;
       case FM_ADDHL: {
-        int p = (opcode >> 4) & 3;
-        int hl = s.HL(), rr = s.getp(p), sum = hl + rr;
+        const int hl = s.HL(), rr = s.getp((opcode >> 4) & 3), sum = hl + rr;
         s.f = FLAGS((s.f >> 7) & 1, 0, ((hl & 0xFFF) + (rr & 0xFFF)) > 0xFFF, sum > 0xFFFF);
         s.setHL(sum);
-        pc += 1; cyc = 8; break;
+        cyc = 8; break;
       }
-      case FM_JR: pc = pc + 2 + sign8(imm8); cyc = 12; break;
-      case FM_JRCC: {
-        const bool t = s.cond(y);
-        pc = pc + 2 + (t ? sign8(imm8) : 0);
+      case FM_JR: {
+        const bool t = opcode == 0x18 || s.cond(y);
+        npc = pc + 2 + (t ? sign8(imm8) : 0);
         cyc = t ? 12 : 8;
         break;
       }
@@ -1047,68 +1031,71 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
           a = (a - adj) & 0xFF;
         }
         s.f = FLAGS(a == 0, n, 0, carry); s.setA(a);
-        pc += 1; break;
+        break;
       }
-      case FM_CPL: s.setA(s.A() ^ 0xFF); s.f = FLAGS((s.f >> 7) & 1, 1, 1, (s.f >> 4) & 1); pc += 1; break;
-      case FM_SCF: s.f = FLAGS((s.f >> 7) & 1, 0, 0, 1); pc += 1; break;
-      case FM_CCF: s.f = FLAGS((s.f >> 7) & 1, 0, 0, !((s.f >> 4) & 1)); pc += 1; break;
-      case FM_LDRR: s.setr(y, s.getr(z)); pc += 1; break;
-      case FM_LDR_HL: s.setr(y, v1); pc += 1; cyc = 8; break;
-      case FM_STHL_R: nw = 1; wa0 = s.HL(); wv0 = s.getr(z); pc += 1; cyc = 8; break;
-      case FM_HALT: s.halted = 1; s.ev |= EV_HALT; pc += 1; break;
-      case FM_ALU_R: s.alu(y, s.getr(z)); pc += 1; break;
+      case FM_FLAGOP: {  // CPL (y=5), SCF (y=6), CCF (y=7)
+        const int zf = (s.f >> 7) & 1, cf = (s.f >> 4) & 1;
+        if (y == 5) { s.setA(s.A() ^ 0xFF); s.f = FLAGS(zf, 1, 1, cf); }
+        else s.f = FLAGS(zf, 0, 0, y == 6 ? 1 : !cf);
+        break;
+      }
+      case FM_LDR_HL: s.setr(y, v1); cyc = 8; break;
+      case FM_STHL_R: nw = 1; wa0 = s.HL(); wv0 = s.getr(z); cyc = 8; break;
+      case FM_HALT: s.halted = 1; s.ev |= EV_HALT; break;
+      case FM_ALU_R: s.alu(y, s.getr(z)); break;
       case FM_ALU_V: {
         const bool hl = rmode == RD_HL;
         s.alu(y, hl ? v1 : imm8);
-        pc += hl ? 1 : 2;
+        npc = pc + (hl ? 1 : 2);
         cyc = 8; break;
       }
       case FM_RET:
         if (opcode == 0xC9 || opcode == 0xD9 || s.cond(y)) {
-          pc = v1 | (v2 << 8);
+          npc = v1 | (v2 << 8);
           s.sp = (s.sp + 2) & 0xFFFF;
-          if (opcode == 0xD9) { s.ime = 1; s.ime_delay = 0; s.ime_mask = 0x1F; }
+          if (opcode == 0xD9) { s.ime = 1; s.ime_delay = 0; s.ev |= EV_IRQ; }
           cyc = (opcode & 1) ? 16 : 20;
         } else {
-          pc += 1; cyc = 8;
+          cyc = 8;
         }
         break;
       case FM_POP: {
-        int p = (opcode >> 4) & 3;
+        const int p = (opcode >> 4) & 3;
         if (p == 3) { s.setA(v2); s.f = v1 & 0xF0; }
         else s.setp(p, v1 | (v2 << 8));
         s.sp = (s.sp + 2) & 0xFFFF;
-        pc += 1; cyc = 12; break;
+        cyc = 12; break;
       }
-      case FM_JP: {
-        const bool t = opcode == 0xC3 || s.cond(y);
-        pc = t ? imm16 : pc + 3;
-        cyc = t ? 16 : 12;
+      case FM_JP:
+        if (opcode == 0xE9) { npc = s.HL(); break; }
+        {
+          const bool t = opcode == 0xC3 || s.cond(y);
+          npc = t ? imm16 : pc + 3;
+          cyc = t ? 16 : 12;
+        }
         break;
-      }
-      case FM_JPHL: pc = s.HL(); break;
       case FM_CALL:
         if (opcode == 0xCD || s.cond(y)) {
-          int ret = (pc + 3) & 0xFFFF;
+          const int ret = (pc + 3) & 0xFFFF;
           nw = 2; wa0 = (s.sp - 1) & 0xFFFF; wv0 = ret >> 8; wa1 = (s.sp - 2) & 0xFFFF; wv1 = ret & 0xFF;
           s.sp = (s.sp - 2) & 0xFFFF;
-          pc = imm16; cyc = 24;
+          npc = imm16; cyc = 24;
         } else {
-          pc += 3; cyc = 12;
+          npc = pc + 3; cyc = 12;
         }
         break;
       case FM_PUSH: {
-        int p = (opcode >> 4) & 3;
-        int v = p == 3 ? ((s.A() << 8) | (s.f & 0xF0)) : s.getp(p);
+        const int p = (opcode >> 4) & 3;
+        const int v = p == 3 ? ((s.A() << 8) | (s.f & 0xF0)) : s.getp(p);
         nw = 2; wa0 = (s.sp - 1) & 0xFFFF; wv0 = v >> 8; wa1 = (s.sp - 2) & 0xFFFF; wv1 = v & 0xFF;
         s.sp = (s.sp - 2) & 0xFFFF;
-        pc += 1; cyc = 16; break;
+        cyc = 16; break;
       }
       case FM_RST: {
-        int ret = (pc + 1) & 0xFFFF;
+        const int ret = (pc + 1) & 0xFFFF;
         nw = 2; wa0 = (s.sp - 1) & 0xFFFF; wv0 = ret >> 8; wa1 = (s.sp - 2) & 0xFFFF; wv1 = ret & 0xFF;
         s.sp = (s.sp - 2) & 0xFFFF;
-        pc = opcode & 0x38; cyc = 16; break;
+        npc = opcode & 0x38; cyc = 16; break;
       }
       case FM_CB: {
         // bitops.py: all 256 CB ops, branch-free over the group
@@ -1125,78 +1112,58 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
         const int res = grp == 0 ? sh : grp == 2 ? (v & ~mask) : (v | mask);
         if (grp == 0) s.f = FLAGS(res == 0, 0, 0, shc);
         if (grp == 1) s.f = FLAGS((v & mask) == 0, 0, 1, oc);
-        pc += 2;
+        npc = pc + 2;
         if (grp == 1) { cyc = hl ? 12 : 8; break; }
         if (hl) { nw = 1; wa0 = s.HL(); wv0 = res; cyc = 16; }
         else { s.setr(cz, res); cyc = 8; }
         break;
       }
-      case FM_ST_A_IO:
-        nw = 1; wv0 = s.A();
-        if (opcode == 0xE0) { wa0 = 0xFF00 | imm8; pc += 2; cyc = 12; }
-        else if (opcode == 0xE2) { wa0 = 0xFF00 | s.C_(); pc += 1; cyc = 8; }
-        else { wa0 = imm16; pc += 3; cyc = 16; }
+      case FM_SPADD:
+        if (opcode == 0xF9) { s.sp = s.HL(); cyc = 8; break; }
+        {
+          const int ou = imm8, res = (s.sp + sign8(imm8)) & 0xFFFF;
+          s.f = FLAGS(0, 0, ((s.sp & 0xF) + (ou & 0xF)) > 0xF, ((s.sp & 0xFF) + ou) > 0xFF);
+          if (opcode == 0xE8) { s.sp = res; cyc = 16; }
+          else { s.setHL(res); cyc = 12; }
+          npc = pc + 2;
+        }
         break;
-      case FM_LD_A_IO:
-        s.setA(v1);
-        if (opcode == 0xF0) { pc += 2; cyc = 12; }
-        else if (opcode == 0xF2) { pc += 1; cyc = 8; }
-        else { pc += 3; cyc = 16; }
+      case FM_IME:
+        s.ime_delay = 0;
+        if (opcode == 0xFB) { s.ime = 1; s.ev |= EV_IRQ; }
+        else s.ime = 0;
         break;
-      case FM_SPADD: {
-        int ou = imm8, res = (s.sp + sign8(imm8)) & 0xFFFF;
-        s.f = FLAGS(0, 0, ((s.sp & 0xF) + (ou & 0xF)) > 0xF, ((s.sp & 0xFF) + ou) > 0xFF);
-        if (opcode == 0xE8) { s.sp = res; cyc = 16; }
-        else { s.setHL(res); cyc = 12; }
-        pc += 2; break;
-      }
-      case FM_LDSPHL: s.sp = s.HL(); pc += 1; cyc = 8; break;
-      case FM_DI: s.ime = 0; s.ime_delay = 0; s.ime_mask = 0; pc += 1; break;
-      case FM_EI: s.ime = 1; s.ime_delay = 0; s.ime_mask = 0x1F; pc += 1; break;
       default:  // FM_TRAP (misc.py:42-56)
         s.trap = 1;
         s.ev |= EV_TRAP;
         st.i32[(size_t)F_TRAP_PC * S + env] = pc & 0xFFFF;
         st.i32[(size_t)F_TRAP_OPCODE * S + env] = opcode & 0xFF;
         st.i32[(size_t)F_TRAP_KIND * S + env] = 1;
+        npc = pc;
         cyc = 0;
         break;
     }
-    s.pc = pc & 0xFFFF;
+    s.pc = npc & 0xFFFF;
     // ---- memory writes ----
     if (nw) {
       s.write8(wa0, wv0);
       if (nw == 2) s.write8(wa1, wv1);
     }
-    // ---- post-processing ----
-    if (s.ev) {
-      if (s.trap) break;
-      instr++;
-      slow_post(s, cyc, opcode, pc_before, 0, frames_to_run, cycle_frame, cyc_total);
-      continue;
-    }
-    instr++;
-    s.t_acc += cyc;
-    if (s.t_acc >= s.t_next) s.timer_sync();
-    s.ppu_lazy(cyc);
-    if (s.ie & s.iflag & s.ime_mask) {
-      slow_post(s, cyc, opcode, pc_before, 1, frames_to_run, cycle_frame, cyc_total);
-      continue;
-    }
-    if (MBC == MBC_MBC3) {
-      if (s.rtc_sub + (cyc & s.rtc_run) >= RTC_CPS) s.rtc_tick(cyc);
-      else s.rtc_sub += cyc & s.rtc_run;
-    }
-    cyc_total += cyc;
-    cycle_frame += cyc;
-    if (cycle_frame >= CYCLES_PER_FRAME) {
-      do {
-        cycle_frame -= CYCLES_PER_FRAME;
-        s.frames_done++;
-      } while (cycle_frame >= CYCLES_PER_FRAME && s.frames_done < frames_to_run);
+    // ---- tail ----
+    if (s.ev & EV_TRAP) break;
+    s.ninstr++;
+    s.clk += cyc;
+    if (s.clk >= s.next_ev || s.ev) {
+      s.slow_post(cyc, opcode, pc, frames_to_run);
+      while (s.halted && s.frames_done < frames_to_run) {
+        s.materialize();
+        s.halted_step(frames_to_run);
+        s.delazify();
+      }
+      if (s.frames_done >= frames_to_run) break;
     }
   }
-  s.materialize();
+  s.sync_all();
 
   // ---- post-step body (post_step.py:11-102) ----
   const int a = s.A(), b = s.getr(0), c = s.getr(1), d = s.getr(2);
@@ -1233,15 +1200,15 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
   stv(F_PC, s.pc & 0xFFFF); stv(F_SP, s.sp & 0xFFFF);
   stv(F_A, a); stv(F_B, b); stv(F_C, c); stv(F_D, d); stv(F_E, e_); stv(F_H, h); stv(F_L, l);
   stv(F_F, s.f & 0xF0);
-  stv(F_CYCLE_IN_FRAME, cycle_frame);
+  stv(F_CYCLE_IN_FRAME, s.cycle_frame);
   stv(F_TRAP_FLAG, s.trap);
   stv(F_IME, s.ime); stv(F_IME_DELAY, s.ime_delay); stv(F_HALTED, s.halted);
   stv(F_DIV_COUNTER, s.div); stv(F_TIMER_PREV_IN, s.prev_in);
   stv(F_TIMA_RELOAD_PENDING, s.rl_pending); stv(F_TIMA_RELOAD_DELAY, s.rl_delay);
   stv(F_PPU_SCANLINE_CYCLE, s.scan); stv(F_PPU_LY, s.ly); stv(F_PPU_WINDOW_LINE, s.wl);
   st.u8s[(size_t)F_STAT_PREV * S + env] = (uint8_t)s.stat_prev;
-  st.i64[(size_t)F_INSTR_COUNT * S + env] = instr;
-  st.i64[(size_t)F_CYCLE_COUNT * S + env] = cyc_total;
+  st.i64[(size_t)F_INSTR_COUNT * S + env] += s.ninstr;
+  st.i64[(size_t)F_CYCLE_COUNT * S + env] += s.cyc_run;
   s.M(0xFF00) = (uint8_t)s.joyp; s.M(0xFF04) = (uint8_t)s.div_b; s.M(0xFF05) = (uint8_t)s.tima;
   s.M(0xFF06) = (uint8_t)s.tma; s.M(0xFF07) = (uint8_t)s.tac; s.M(0xFF0F) = (uint8_t)s.iflag;
   s.M(0xFF40) = (uint8_t)s.lcdc; s.M(0xFF41) = (uint8_t)s.stat; s.M(0xFF44) = (uint8_t)s.ly_b;
@@ -1268,52 +1235,60 @@ __global__ void __launch_bounds__(256, REGCAP ? 4 : 1)
 // ---------------------------------------------------------------------------
 // Host launcher
 // ---------------------------------------------------------------------------
-size_t step_smem_bytes(const DevState& st) {
-  int r = st.rom_bytes < ROM_SMEM_MAX ? st.rom_bytes : ROM_SMEM_MAX;
-  return 768 + (size_t)((r + 15) & ~15);
-}
-
 static int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
   return v && *v ? atoi(v) : dflt;
 }
 
-// Envs per warp and register cap for a batch of n envs (overridable with
-// GBX_ENVS_PER_WARP / GBX_STEP_REGCAP for measurements).
-void step_launch_shape(int n, int* K, int* regcap) {
+// Envs per warp for a batch of n envs (GBX_ENVS_PER_WARP overrides). Few
+// envs: spread them (one env per warp hides latency, no divergence); many
+// envs: pack them so every SM stays within one resident wave.
+int step_envs_per_warp(int n) {
   int k = env_int("GBX_ENVS_PER_WARP", 0);
-  int rc = env_int("GBX_STEP_REGCAP", -1);
-  if (k <= 0) k = 32;
-  if (k > 32) k = 32;
-  *K = k;
-  *regcap = rc < 0 ? 0 : (rc ? 1 : 0);
+  if (k > 0) return k > 32 ? 32 : k;
+  const long long slots = 148LL * 28;  // resident warps per GPU at this kernel's footprint
+  k = 1;
+  while (k < 32 && (n + k - 1) / k > slots) k *= 2;
+  return k;
 }
 
-template <int MBC>
-static cudaError_t launch_mbc(const DevState& st, const int32_t* actions, int frames, int release, int stage,
-                              cudaStream_t stream, int K, int regcap, size_t sm) {
-  const int threads = 256;
-  const long long warps = (st.n + K - 1) / K;
-  const int blocks = (int)((warps * 32 + threads - 1) / threads);
-  if (regcap) {
-    cudaFuncSetAttribute(gb_step_kernel<MBC, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    gb_step_kernel<MBC, 1><<<blocks, threads, sm, stream>>>(st, actions, frames, release, stage, K);
-  } else {
-    cudaFuncSetAttribute(gb_step_kernel<MBC, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-    gb_step_kernel<MBC, 0><<<blocks, threads, sm, stream>>>(st, actions, frames, release, stage, K);
-  }
+template <int MBC, int MAXT>
+static cudaError_t launch_t(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames,
+                            int release, int stage, cudaStream_t stream, int K, int threads, int blocks,
+                            int pre_s_words, size_t sm) {
+  cudaError_t e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sm);
+  if (e != cudaSuccess) return e;
+  gb_step_kernel<MBC, MAXT><<<blocks, threads, sm, stream>>>(st, pre, actions, frames, release, stage, K,
+                                                            pre_s_words);
   return cudaGetLastError();
 }
 
-cudaError_t launch_step(const DevState& st, const int32_t* actions, int frames, int release, int stage,
-                        cudaStream_t stream) {
-  const size_t sm = step_smem_bytes(st);
-  int K, regcap;
-  step_launch_shape(st.n, &K, &regcap);
+template <int MBC>
+static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames,
+                              int release, int stage, cudaStream_t stream) {
+  const int K = step_envs_per_warp(st.n);
+  const long long warps = (st.n + K - 1) / K;
+  // one block per SM (the pre-decoded banks fill shared memory): spread warps
+  int per_block = (int)((warps + 147) / 148);
+  per_block = per_block < 1 ? 1 : per_block > 32 ? 32 : per_block;
+  const int threads = per_block * 32;
+  const int blocks = (int)((warps + per_block - 1) / per_block);
+  const int rom_words = st.rom_bytes < ROM_SMEM_MAX ? st.rom_bytes : ROM_SMEM_MAX;
+  const size_t sm = (size_t)rom_words * 4 + 512;
+  if (threads <= 256)
+    return launch_t<MBC, 256>(st, pre, actions, frames, release, stage, stream, K, threads, blocks, rom_words, sm);
+  if (threads <= 512)
+    return launch_t<MBC, 512>(st, pre, actions, frames, release, stage, stream, K, threads, blocks, rom_words, sm);
+  return launch_t<MBC, 1024>(st, pre, actions, frames, release, stage, stream, K, threads, blocks, rom_words, sm);
+}
+
+cudaError_t launch_step(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames, int release,
+                        int stage, cudaStream_t stream) {
   switch (st.mbc_kind) {
-    case MBC_MBC1: return launch_mbc<MBC_MBC1>(st, actions, frames, release, stage, stream, K, regcap, sm);
-    case MBC_MBC3: return launch_mbc<MBC_MBC3>(st, actions, frames, release, stage, stream, K, regcap, sm);
-    default: return launch_mbc<MBC_ROM_ONLY>(st, actions, frames, release, stage, stream, K, regcap, sm);
+    case MBC_MBC1: return launch_mbc<MBC_MBC1>(st, pre, actions, frames, release, stage, stream);
+    case MBC_MBC3: return launch_mbc<MBC_MBC3>(st, pre, actions, frames, release, stage, stream);
+    default: return launch_mbc<MBC_ROM_ONLY>(st, pre, actions, frames, release, stage, stream);
   }
 }
 
