@@ -322,8 +322,8 @@ class GbxVecCudaBackend:
     def memory_torch(self):
         """[N, 65536] uint8 zero-copy view of device memory (warp_vec.py:799-810).
 
-        The view is strided (env stride 1, address stride S): device memory is
-        address-major so lockstep warps coalesce.
+        Device memory is env-major, so the view is contiguous like the
+        reference's.
         """
         self._need()
         return self._view("mem")

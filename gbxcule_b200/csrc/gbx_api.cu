@@ -22,10 +22,6 @@ cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset,
 cudaError_t launch_init(const DevState& st, cudaStream_t s);
 cudaError_t launch_snapshot(const DevState& st, const Snapshot& snap, int env, cudaStream_t s);
 cudaError_t launch_restore(const DevState& st, const Snapshot& snap, const uint8_t* mask, cudaStream_t s);
-cudaError_t launch_to_env_major(const uint8_t* src, uint8_t* dst, int rows, int S, int lo, int hi,
-                                cudaStream_t s);
-cudaError_t launch_from_env_major(const uint8_t* src, uint8_t* dst, int rows, int S, int lo, int hi,
-                                  cudaStream_t s);
 }  // namespace gbx
 
 using namespace gbx;
@@ -42,8 +38,6 @@ struct gbx_env {
   uint8_t* pix;
   uint8_t* pix_packed;
   uint32_t* pre;           // pre-decoded ROM, one word per byte (gbx_step.cu)
-  uint8_t* staging;        // device staging for layout conversion
-  size_t staging_bytes;
   bool initialized;
 };
 
@@ -131,18 +125,17 @@ int dalloc(T** p, size_t count) {
 void free_env(gbx_env* h) {
   DevState& st = h->st;
   void* ptrs[] = {(void*)st.rom, (void*)st.boot, st.mem, st.cart_ram, st.serial, st.cart_state, st.i32,
-                  st.i64, st.u8s, st.latch, st.obs, st.reward, st.status, h->pix, h->pix_packed, h->staging,
-                  h->pre};
+                  st.i64, st.u8s, st.latch, st.obs, st.reward, st.status, h->pix, h->pix_packed, h->pre};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
 
 int zero_state(gbx_env* h, cudaStream_t s) {
   DevState& st = h->st;
-  const size_t S = st.S;
-  CK(cudaMemsetAsync(st.mem, 0, (size_t)MEM_SIZE * S, s), "memset mem");
-  CK(cudaMemsetAsync(st.cart_ram, 0, (size_t)h->ram_rows * S, s), "memset cart_ram");
-  CK(cudaMemsetAsync(st.serial, 0, (size_t)SERIAL_MAX * S, s), "memset serial");
+  const size_t S = st.S, n = st.n;
+  CK(cudaMemsetAsync(st.mem, 0, (size_t)MEM_SIZE * n, s), "memset mem");
+  CK(cudaMemsetAsync(st.cart_ram, 0, (size_t)h->ram_rows * n, s), "memset cart_ram");
+  CK(cudaMemsetAsync(st.serial, 0, (size_t)SERIAL_MAX * n, s), "memset serial");
   CK(cudaMemsetAsync(st.cart_state, 0, sizeof(int32_t) * CS_STRIDE * S, s), "memset cart_state");
   CK(cudaMemsetAsync(st.i32, 0, sizeof(int32_t) * I32_COUNT * S, s), "memset i32");
   CK(cudaMemsetAsync(st.i64, 0, sizeof(int64_t) * I64_COUNT * S, s), "memset i64");
@@ -171,26 +164,15 @@ int check_range(const gbx_env* h, int lo, int hi) {
   return GBX_OK;
 }
 
-// interleaved rows [rows][S] -> host env-major [hi-lo][rows], chunked through staging
-int export_rows(gbx_env* h, const uint8_t* src, int rows, int lo, int hi, uint8_t* host) {
-  const int per = (int)(h->staging_bytes / (size_t)rows);
-  for (int e = lo; e < hi; e += per) {
-    int e1 = e + per < hi ? e + per : hi;
-    CK(launch_to_env_major(src, h->staging, rows, h->st.S, e, e1, 0), "to_env_major");
-    CK(cudaMemcpy(host + (size_t)(e - lo) * rows, h->staging, (size_t)(e1 - e) * rows, cudaMemcpyDeviceToHost),
-       "export copy");
-  }
+// env-major byte arrays [n][rows]: envs [lo, hi) are one contiguous range
+int export_rows(const uint8_t* src, int rows, int lo, int hi, uint8_t* host) {
+  if (hi > lo)
+    CK(cudaMemcpy(host, src + (size_t)lo * rows, (size_t)(hi - lo) * rows, cudaMemcpyDeviceToHost), "export copy");
   return GBX_OK;
 }
-int import_rows(gbx_env* h, uint8_t* dst, int rows, int lo, int hi, const uint8_t* host) {
-  const int per = (int)(h->staging_bytes / (size_t)rows);
-  for (int e = lo; e < hi; e += per) {
-    int e1 = e + per < hi ? e + per : hi;
-    CK(cudaMemcpy(h->staging, host + (size_t)(e - lo) * rows, (size_t)(e1 - e) * rows, cudaMemcpyHostToDevice),
-       "import copy");
-    CK(launch_from_env_major(h->staging, dst, rows, h->st.S, e, e1, 0), "from_env_major");
-  }
-  CK(cudaDeviceSynchronize(), "import sync");
+int import_rows(uint8_t* dst, int rows, int lo, int hi, const uint8_t* host) {
+  if (hi > lo)
+    CK(cudaMemcpy(dst + (size_t)lo * rows, host, (size_t)(hi - lo) * rows, cudaMemcpyHostToDevice), "import copy");
   return GBX_OK;
 }
 template <class T>
@@ -245,12 +227,13 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
   st.ram_bank_count = ram_bytes / RAM_BANK;
   h->ram_bytes = ram_bytes;
   h->ram_rows = ram_bytes > 0 ? ram_bytes : 1;
-  const size_t S = st.S;
+  st.ram_rows = h->ram_rows;
+  const size_t S = st.S, n = st.n;
   int rc = GBX_OK;
   uint8_t *rom_d = nullptr, *boot_d = nullptr;
   if ((rc = dalloc(&rom_d, (size_t)rom_bytes)) || (rc = dalloc(&boot_d, 256)) ||
-      (rc = dalloc(&st.mem, (size_t)MEM_SIZE * S)) || (rc = dalloc(&st.cart_ram, (size_t)h->ram_rows * S)) ||
-      (rc = dalloc(&st.serial, (size_t)SERIAL_MAX * S)) || (rc = dalloc(&st.cart_state, (size_t)CS_STRIDE * S)) ||
+      (rc = dalloc(&st.mem, (size_t)MEM_SIZE * n)) || (rc = dalloc(&st.cart_ram, (size_t)h->ram_rows * n)) ||
+      (rc = dalloc(&st.serial, (size_t)SERIAL_MAX * n)) || (rc = dalloc(&st.cart_state, (size_t)CS_STRIDE * S)) ||
       (rc = dalloc(&st.i32, (size_t)I32_COUNT * S)) || (rc = dalloc(&st.i64, (size_t)I64_COUNT * S)) ||
       (rc = dalloc(&st.u8s, (size_t)U8_COUNT * S)) || (rc = dalloc(&st.latch, 9 * SCREEN_H)) ||
       (rc = dalloc(&st.obs, (size_t)OBS_DIM * st.n)) || (rc = dalloc(&st.reward, (size_t)st.n)) ||
@@ -265,12 +248,6 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
   }
   st.rom = rom_d;
   st.boot = boot_d;
-  h->staging_bytes = (size_t)64 << 20;
-  if ((rc = dalloc(&h->staging, h->staging_bytes))) {
-    free_env(h);
-    delete h;
-    return rc;
-  }
   if ((rc = dalloc(&h->pre, (size_t)rom_bytes))) {
     free_env(h);
     delete h;
@@ -385,14 +362,16 @@ int gbx_snapshot_create(gbx_env* h, int32_t env_idx, void* stream, gbx_snapshot*
     delete sn;
     return cuda_fail(e, "snapshot alloc");
   }
+  // byte blocks first so each starts 16-byte aligned (cart RAM sizes are
+  // multiples of 16 or a single byte)
   uint8_t* p = static_cast<uint8_t*>(sn->block);
+  sn->s.mem = p; p += MEM_SIZE;
+  sn->s.serial = p; p += SERIAL_MAX;
+  sn->s.cart_ram = p; p += (h->ram_rows + 15) & ~15;
   sn->s.i64 = reinterpret_cast<int64_t*>(p); p += 8 * I64_COUNT;
   sn->s.cart_state = reinterpret_cast<int32_t*>(p); p += 4 * CS_STRIDE;
   sn->s.i32 = reinterpret_cast<int32_t*>(p); p += 4 * I32_COUNT;
-  sn->s.u8s = p; p += U8_COUNT;
-  sn->s.mem = p; p += MEM_SIZE;
-  sn->s.serial = p; p += SERIAL_MAX;
-  sn->s.cart_ram = p;
+  sn->s.u8s = p;
   sn->s.ram_bytes = h->ram_rows;
   sn->device = h->cfg.device;
   e = launch_snapshot(h->st, sn->s, env_idx, S_(stream));
@@ -437,7 +416,7 @@ int gbx_buffer(const gbx_env* h, int32_t which, gbx_buffer_info* o) {
     o->strides[0] = t0; o->strides[1] = t1; o->strides[2] = t2;
   };
   switch (which) {
-    case GBX_BUF_MEM: set(st.mem, 1, 8, 2, n, MEM_SIZE, 0, 1, S, 0); break;
+    case GBX_BUF_MEM: set(st.mem, 1, 8, 2, n, MEM_SIZE, 0, MEM_SIZE, 1, 0); break;
     case GBX_BUF_PIXELS:
       if (!h->pix) return fail(GBX_ERR_STATE, "Pixel buffer not initialized. Call reset() first.");
       set(h->pix, 1, 8, 3, n, 72, 80, SHADE_BYTES, 80, 1); break;
@@ -446,8 +425,8 @@ int gbx_buffer(const gbx_env* h, int32_t which, gbx_buffer_info* o) {
       set(h->pix_packed, 1, 8, 3, n, 72, 20, PACKED_BYTES, 20, 1); break;
     case GBX_BUF_OBS: set(st.obs, 2, 32, 2, n, OBS_DIM, 0, OBS_DIM, 1, 0); break;
     case GBX_BUF_REWARD: set(st.reward, 2, 32, 1, n, 0, 0, 1, 0, 0); break;
-    case GBX_BUF_CART_RAM: set(st.cart_ram, 1, 8, 2, n, h->ram_rows, 0, 1, S, 0); break;
-    case GBX_BUF_SERIAL: set(st.serial, 1, 8, 2, n, SERIAL_MAX, 0, 1, S, 0); break;
+    case GBX_BUF_CART_RAM: set(st.cart_ram, 1, 8, 2, n, h->ram_rows, 0, h->ram_rows, 1, 0); break;
+    case GBX_BUF_SERIAL: set(st.serial, 1, 8, 2, n, SERIAL_MAX, 0, SERIAL_MAX, 1, 0); break;
     case GBX_BUF_I32: set(st.i32, 0, 32, 2, I32_COUNT, n, 0, S, 1, 0); break;
     case GBX_BUF_I64: set(st.i64, 0, 64, 2, I64_COUNT, n, 0, S, 1, 0); break;
     case GBX_BUF_U8: set(st.u8s, 1, 8, 2, U8_COUNT, n, 0, S, 1, 0); break;
@@ -495,9 +474,9 @@ int gbx_export_state(gbx_env* h, int32_t lo, int32_t hi, const gbx_host_state* o
   CK(cudaDeviceSynchronize(), "sync before export");
   const DevState& st = h->st;
   const size_t S = st.S;
-  if (o->mem) RET(export_rows(h, st.mem, MEM_SIZE, lo, hi, o->mem));
-  if (o->cart_ram) RET(export_rows(h, st.cart_ram, h->ram_rows, lo, hi, o->cart_ram));
-  if (o->serial) RET(export_rows(h, st.serial, SERIAL_MAX, lo, hi, o->serial));
+  if (o->mem) RET(export_rows(st.mem, MEM_SIZE, lo, hi, o->mem));
+  if (o->cart_ram) RET(export_rows(st.cart_ram, h->ram_rows, lo, hi, o->cart_ram));
+  if (o->serial) RET(export_rows(st.serial, SERIAL_MAX, lo, hi, o->serial));
   if (o->cart_state) RET(copy_fields(st.cart_state, CS_STRIDE, S, lo, hi, o->cart_state, true));
   if (o->i32) RET(copy_fields(st.i32, I32_COUNT, S, lo, hi, o->i32, true));
   if (o->i64) RET(copy_fields(st.i64, I64_COUNT, S, lo, hi, o->i64, true));
@@ -519,9 +498,9 @@ int gbx_import_state(gbx_env* h, int32_t lo, int32_t hi, const gbx_host_state* i
   CK(cudaDeviceSynchronize(), "sync before import");
   const DevState& st = h->st;
   const size_t S = st.S;
-  if (in->mem) RET(import_rows(h, st.mem, MEM_SIZE, lo, hi, in->mem));
-  if (in->cart_ram) RET(import_rows(h, st.cart_ram, h->ram_rows, lo, hi, in->cart_ram));
-  if (in->serial) RET(import_rows(h, st.serial, SERIAL_MAX, lo, hi, in->serial));
+  if (in->mem) RET(import_rows(st.mem, MEM_SIZE, lo, hi, in->mem));
+  if (in->cart_ram) RET(import_rows(st.cart_ram, h->ram_rows, lo, hi, in->cart_ram));
+  if (in->serial) RET(import_rows(st.serial, SERIAL_MAX, lo, hi, in->serial));
   if (in->cart_state) RET(copy_fields(st.cart_state, CS_STRIDE, S, lo, hi, in->cart_state, false));
   if (in->i32) RET(copy_fields(st.i32, I32_COUNT, S, lo, hi, in->i32, false));
   if (in->i64) RET(copy_fields(st.i64, I64_COUNT, S, lo, hi, in->i64, false));
@@ -546,9 +525,8 @@ int gbx_read_mem(gbx_env* h, int32_t env_idx, int32_t lo, int32_t hi, uint8_t* h
   if (!host_out) return fail(GBX_ERR_INVALID, "null out");
   DeviceGuard g(h->cfg.device);
   CK(cudaDeviceSynchronize(), "sync before read");
-  const uint8_t* src = h->st.mem + (size_t)lo * h->st.S;
-  CK(launch_to_env_major(src, h->staging, hi - lo, h->st.S, env_idx, env_idx + 1, 0), "to_env_major");
-  CK(cudaMemcpy(host_out, h->staging, (size_t)(hi - lo), cudaMemcpyDeviceToHost), "read copy");
+  const uint8_t* src = h->st.mem + (size_t)env_idx * MEM_SIZE + lo;
+  CK(cudaMemcpy(host_out, src, (size_t)(hi - lo), cudaMemcpyDeviceToHost), "read copy");
   return GBX_OK;
 }
 

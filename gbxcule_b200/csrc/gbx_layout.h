@@ -1,11 +1,13 @@
 // gbx_layout.h - device-side data layout shared by every kernel of libgbx.
 //
-// HBM layout (one allocation set per handle, S = env stride, a multiple of 32):
-//   mem        u8  [65536][S]  byte a of env e at mem[a*S + e] (address-major,
-//                               env-minor: a warp touching one address reads
-//                               one 32-byte sector)
-//   cart_ram   u8  [ram_bytes][S]       same interleaving
-//   serial     u8  [1024][S]
+// HBM layout (one allocation set per handle; S = SoA row stride, n rounded up
+// to a multiple of 128):
+//   mem        u8  [N][65536]           env-major: env e's address space is
+//                                       one contiguous 64 KiB block, exactly
+//                                       the reference's mem view
+//                                       (warp_vec.py:799-810)
+//   cart_ram   u8  [N][ram_rows]        env-major (ram_rows = max(ram_bytes, 1))
+//   serial     u8  [N][1024]            env-major
 //   cart_state i32 [20][S]              field-major (SoA)
 //   i32        i32 [I32_COUNT][S]       one row per scalar field (SoA)
 //   i64        i64 [2][S]               instr_count, cycle_count
@@ -13,8 +15,12 @@
 //   latch      u8  [9][144]             env-0 scanline latches
 //   obs        f32 [N][32], reward f32 [N]   (reference layout, torch views)
 //   pix_packed u8  [N][72][20], pix u8 [N][72][80]
-// The reference keeps the same fields env-major (warp_vec.py:279-497); the
-// host API converts when it exports state.
+// Env-major byte arrays keep every env's stack, HRAM and IO page in lines of
+// its own: an interleaved layout makes the warps of neighbouring envs write
+// single bytes of one shared sector, and read-after-write on the stack then
+// serialises in L2. The per-env scalars are only touched at the start and end
+// of a launch, so they stay SoA; the host API converts them when it exports
+// state (the reference keeps them env-major, warp_vec.py:279-497).
 #pragma once
 #include <stdint.h>
 
@@ -66,7 +72,8 @@ struct DevState {
   const uint8_t* rom;     // [rom_bytes] shared, read-only
   const uint8_t* boot;    // [256]
   int32_t rom_bytes, rom_bank_count, rom_bank_mask, ram_bank_count;
-  int32_t n, S;           // envs, env stride
+  int32_t n, S;           // envs, SoA row stride
+  int32_t ram_rows;       // cart_ram bytes per env (>= 1)
   int32_t mbc_kind;
   uint8_t* mem;
   uint8_t* cart_ram;

@@ -9,8 +9,9 @@
 // instruction; here that state lives in registers for the whole launch and
 // goes back to HBM once at the end.
 //
-//  * Memory: address-major, env-minor (gbx_layout.h), so lockstep warps
-//    coalesce. Cached IO ports (JOYP, DIV, TIMA, TMA, TAC, IF, LCDC, STAT, LY,
+//  * Memory: env-major (gbx_layout.h): each env's stack, HRAM and IO page sit
+//    in cache lines of their own, so envs on different warps never write the
+//    same sector. Cached IO ports (JOYP, DIV, TIMA, TMA, TAC, IF, LCDC, STAT, LY,
 //    LYC, WY, IE) live in registers; every path that touches those addresses
 //    (CPU access, OAM DMA source, env-0 latches) goes through the cache.
 //  * Fetch: the ROM is pre-decoded on the host into one 32-bit word per byte
@@ -139,15 +140,15 @@ enum Event { EV_FIRST = 1, EV_HALT = 2, EV_TRAP = 4, EV_LCDC = 8, EV_PPU = 16, E
 template <int MBC>
 struct Emu {
   // addressing
-  uint8_t* mem;           // &st.mem[env]; byte a at mem[a * S]
-  uint32_t S;
+  uint8_t* mem;           // env's 64 KiB address space (env-major)
+  uint32_t S;             // SoA row stride of the scalar fields
   const uint32_t* pre_s;  // shared memory: pre-decoded rom[0 .. pre_s_words)
   const uint32_t* pre_g;  // global pre-decoded ROM
   const uint8_t* boot_s;  // shared memory: boot ROM
   const uint8_t* rom_g;   // global ROM bytes
   int32_t* cart_state;    // &st.cart_state[env]
-  uint8_t* cart_ram;      // &st.cart_ram[env]
-  uint8_t* serial;        // &st.serial[env]
+  uint8_t* cart_ram;      // env's cartridge RAM (env-major)
+  uint8_t* serial;        // env's serial capture buffer (env-major)
   int32_t* i32;           // &st.i32[env]
   uint8_t* u8s;           // &st.u8s[env]
   uint8_t* latch;         // st.latch
@@ -207,7 +208,7 @@ struct Emu {
   }
 
   // ---- memory -------------------------------------------------------------
-  __device__ __forceinline__ uint8_t& M(int a) const { return mem[(size_t)a * S]; }
+  __device__ __forceinline__ uint8_t& M(int a) const { return mem[a]; }
 
   __device__ __forceinline__ void update_banks() {
     // cpu_step_builder.py:566-592 (bank selection and clamp_bank)
@@ -302,7 +303,7 @@ struct Emu {
     }
     int off = ram_index(a);
     if (off < 0) return 0xFF;
-    return cart_ram[(size_t)off * S];
+    return cart_ram[off];
   }
 
   // read8 (:539-657); region = a >> 13: 4 VRAM and 6 WRAM first
@@ -527,7 +528,7 @@ struct Emu {
         if ((val & 0x80) && (val & 0x01)) {
           int idx = i32[(size_t)F_SERIAL_LEN * S];
           if (idx < SERIAL_MAX) {
-            serial[(size_t)idx * S] = M(0xFF01);
+            serial[idx] = M(0xFF01);
             i32[(size_t)F_SERIAL_LEN * S] = idx + 1;
           } else {
             u8s[(size_t)F_SERIAL_OVERFLOW * S] = 1;
@@ -615,7 +616,7 @@ struct Emu {
         }
       }
       int off = ram_index(a);
-      if (off >= 0) cart_ram[(size_t)off * S] = (uint8_t)v8;
+      if (off >= 0) cart_ram[off] = (uint8_t)v8;
       return;
     }
     if (a < 0x8000) {
@@ -824,15 +825,15 @@ __global__ void __launch_bounds__(MAXT, 1)
   const size_t S = (size_t)st.S;
 
   Emu<MBC> s;
-  s.mem = st.mem + env;
+  s.mem = st.mem + (size_t)env * MEM_SIZE;
   s.S = st.S;
   s.pre_s = pre_s;
   s.pre_g = pre_g;
   s.boot_s = boot_s;
   s.rom_g = st.rom;
   s.cart_state = st.cart_state + env;
-  s.cart_ram = st.cart_ram + env;
-  s.serial = st.serial + env;
+  s.cart_ram = st.cart_ram + (size_t)env * st.ram_rows;
+  s.serial = st.serial + (size_t)env * SERIAL_MAX;
   s.i32 = st.i32 + env;
   s.u8s = st.u8s + env;
   s.latch = st.latch;
@@ -1171,8 +1172,12 @@ __global__ void __launch_bounds__(MAXT, 1)
   if (stage == STAGE_OBS || stage == STAGE_FULL) {
     float* o = st.obs + (size_t)env * OBS_DIM;
     int m[16];
+    {
+      const uint4 q16 = *reinterpret_cast<const uint4*>(&s.M(0xC000));  // 16-byte aligned
+      const uint32_t w4[4] = {q16.x, q16.y, q16.z, q16.w};
 #pragma unroll
-    for (int k = 0; k < 16; k++) m[k] = s.M(0xC000 + k);
+      for (int k = 0; k < 16; k++) m[k] = (w4[k >> 2] >> (8 * (k & 3))) & 0xFF;
+    }
     float4 q[8];
     q[0] = make_float4((float)(s.pc & 0xFFFF) / 65535.0f, (float)(s.sp & 0xFFFF) / 65535.0f,
                        (float)a / 255.0f, (float)(s.f & 0xFF) / 255.0f);
@@ -1240,16 +1245,18 @@ static int env_int(const char* name, int dflt) {
   return v && *v ? atoi(v) : dflt;
 }
 
-// Envs per warp for a batch of n envs (GBX_ENVS_PER_WARP overrides). Few
-// envs: spread them (one env per warp hides latency, no divergence); many
-// envs: pack them so every SM stays within one resident wave.
+// Envs per warp for a batch of n envs (GBX_ENVS_PER_WARP overrides).
+// One env per warp has no divergence but leaves 31 lanes idle, so its
+// throughput stops growing once every SM holds a full wave of single-env
+// warps; 32 envs per warp shares every issue slot among the envs that take
+// the same path and keeps growing with n. Measured on B200 (config ROMs,
+// frameskip 24): 4,096 envs run fastest at K = 1, 16,384 and 65,536 at
+// K = 32, intermediate K never beats both. Switch after three waves.
 int step_envs_per_warp(int n) {
   int k = env_int("GBX_ENVS_PER_WARP", 0);
   if (k > 0) return k > 32 ? 32 : k;
-  const long long slots = 148LL * 28;  // resident warps per GPU at this kernel's footprint
-  k = 1;
-  while (k < 32 && (n + k - 1) / k > slots) k *= 2;
-  return k;
+  const long long wave = 148LL * 28;  // resident single-env warps per GPU at this kernel's footprint
+  return n <= 3 * wave ? 1 : 32;
 }
 
 template <int MBC, int MAXT>

@@ -45,13 +45,13 @@ typedef enum {
 
 /* Device buffers exposed for zero-copy views (warp_vec.py:799-901). */
 typedef enum {
-  GBX_BUF_MEM = 0,            /* u8  [n, 65536]   strides [1, S]    */
+  GBX_BUF_MEM = 0,            /* u8  [n, 65536]   contiguous        */
   GBX_BUF_PIXELS = 1,         /* u8  [n, 72, 80]  contiguous        */
   GBX_BUF_PIXELS_PACKED = 2,  /* u8  [n, 72, 20]  contiguous        */
   GBX_BUF_OBS = 3,            /* f32 [n, 32]      contiguous        */
   GBX_BUF_REWARD = 4,         /* f32 [n]                            */
-  GBX_BUF_CART_RAM = 5,       /* u8  [n, ram]     strides [1, S]    */
-  GBX_BUF_SERIAL = 6,         /* u8  [n, 1024]    strides [1, S]    */
+  GBX_BUF_CART_RAM = 5,       /* u8  [n, max(ram,1)] contiguous     */
+  GBX_BUF_SERIAL = 6,         /* u8  [n, 1024]    contiguous        */
   GBX_BUF_I32 = 7,            /* i32 [GBX_I32_COUNT, n] strides [S, 1] */
   GBX_BUF_I64 = 8,            /* i64 [2, n]       strides [S, 1]    */
   GBX_BUF_U8 = 9,             /* u8  [3, n]       strides [S, 1]    */
