@@ -200,6 +200,8 @@ def run_gbx(args) -> None:
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
+    i64 = be._view("i64")  # row 0: per-env emulated instruction counters
+    ninstr0 = int(i64[0].sum())
     clocks = ClockSampler(local)
     clocks.start()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
@@ -218,6 +220,7 @@ def run_gbx(args) -> None:
     clk = clocks.stop()
     step_ms = [s.elapsed_time(m) for s, m, _ in ev]
     total_ms = sum(s.elapsed_time(e) for s, _, e in ev)
+    ninstr = int(i64[0].sum()) - ninstr0
 
     # end to end through the public API with host buffers
     acts_pin = torch.from_numpy(acts_host[W + K:W + 2 * K]).pin_memory()
@@ -239,9 +242,12 @@ def run_gbx(args) -> None:
     e2e_ms = e0.elapsed_time(e1)
 
     t = torch.tensor([total_ms, e2e_ms, float(np.mean(step_ms))], dtype=torch.float64, device=dev)
+    c = torch.tensor([ninstr], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(c, op=dist.ReduceOp.SUM)
     total_ms, e2e_ms, step_avg_ms = (float(x) for x in t.tolist())
+    ninstr = float(c.item())
     be.close()
     if dist:
         dist.barrier()
@@ -262,6 +268,10 @@ def run_gbx(args) -> None:
                    "obs": "packed 2bpp 72x20 rendered every step", "l2": "flushed between timed steps (256 MiB write)",
                    "parallelism": f"{ws} independent env slices, no collective on the step path"},
         "emulated_frames_per_s": value * FRAMES,
+        # SM83 instructions retired by all envs per second of step-kernel time
+        # (the step kernel is bound by integer issue per emulated instruction)
+        "emulated_instr_per_s": ninstr / (step_avg_ms * K / 1e3),
+        "emulated_instr_per_env_step": ninstr / (total_envs * K),
         "e2e": {"value": total_envs * K / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": 4 * n,
                 "d2h_bytes_per_step": 72 * 20 * n},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
