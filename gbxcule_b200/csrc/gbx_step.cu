@@ -137,47 +137,14 @@ void predecode_rom(const uint8_t* rom, int n, uint32_t* out) {
 enum Event { EV_FIRST = 1, EV_HALT = 2, EV_TRAP = 4, EV_LCDC = 8, EV_PPU = 16, EV_RTC = 32, EV_IRQ = 64,
              EV_TIMER = 128 };
 
-template <int MBC>
-struct Emu {
-  // addressing
-  uint8_t* mem;           // env's 64 KiB address space (env-major)
-  uint32_t S;             // SoA row stride of the scalar fields
-  const uint32_t* pre_s;  // shared memory: pre-decoded rom[0 .. pre_s_words)
-  const uint32_t* pre_g;  // global pre-decoded ROM
-  const uint8_t* boot_s;  // shared memory: boot ROM
-  const uint8_t* rom_g;   // global ROM bytes
-  int32_t* cart_state;    // &st.cart_state[env]
-  uint8_t* cart_ram;      // env's cartridge RAM (env-major)
-  uint8_t* serial;        // env's serial capture buffer (env-major)
-  int32_t* i32;           // &st.i32[env]
-  uint8_t* u8s;           // &st.u8s[env]
-  uint8_t* latch;         // st.latch
-  int rom_bank_count, rom_bank_mask, ram_bank_count;
-  int pre_s_words;
-  int is_env0;
-  // CPU
-  uint32_t bcde, hlxa;   // B C D E | H L - A, high byte first
+// CPU registers and the event clock: the only state the interpreter loop
+// keeps in registers. Everything else lives in Emu, in local memory, and is
+// touched by the out-of-line slow paths only.
+struct Hot {
+  uint32_t bcde, hlxa;  // B C D E | H L - A, high byte first
   int f, pc, sp;
-  int ime, ime_delay, halted;
-  int trap;
-  // cached IO ports (values of mem[FFxx]); stat/div_b/prev_in/stat_prev are
-  // exact only while lazy == 0
-  int joyp, div_b, tima, tma, tac, iflag, lcdc, stat, ly_b, lyc, wy, ie;
-  // timer
-  int div, rl_pending, rl_delay, prev_in;
-  // PPU
-  int scan, ly, wl, stat_prev;
-  // cart
-  int ram_en, bank_lo, bank_hi, ram_bank, bank_mode, bootrom, rtc_sel, rtc_latch;
-  int bank0_off, bankN_off;   // ROM byte offset of a bank region; -1 when out of range
-  int rtc_sub, rtc_s, rtc_m, rtc_h, rtc_dl, rtc_dh;
-  // step
-  int frames_done, release, action;
-  int cycle_frame, cyc_run, ninstr;
-  // lazy state
-  int lazy, ev, clk, next_ev, stat_hi, lcd_on, rtc_run, lcdc_before;
+  int clk, next_ev;     // cycles since the last sync; cycles to the next event
 
-  // ---- registers -------------------------------------------------------
   __device__ __forceinline__ int A() const { return hlxa & 0xFF; }
   __device__ __forceinline__ void setA(int v) { hlxa = (hlxa & 0xFFFFFF00u) | (uint32_t)(v & 0xFF); }
   __device__ __forceinline__ int HL() const { return hlxa >> 16; }
@@ -206,6 +173,79 @@ struct Emu {
     else if (p == 2) hlxa = (hlxa & 0xFFFFu) | ((uint32_t)v << 16);
     else sp = v;
   }
+  // ALU kinds ADD ADC SUB SBC AND XOR OR CP (alu.py)
+  __device__ __forceinline__ void alu(int kind, int v) {
+    const int a = A();
+    int r;
+    switch (kind) {
+      case 0: case 1: {
+        const int cin = kind == 1 ? (f >> 4) & 1 : 0;
+        r = a + v + cin;
+        f = (((r & 0xFF) == 0) << 7) | ((((a & 0xF) + (v & 0xF) + cin) > 0xF) << 5) | ((r > 0xFF) << 4);
+        setA(r);
+        return;
+      }
+      case 2: case 3: case 7: {
+        const int cin = kind == 3 ? (f >> 4) & 1 : 0;
+        r = a - v - cin;
+        f = (((r & 0xFF) == 0) << 7) | 0x40 | ((((a & 0xF) - (v & 0xF) - cin) < 0) << 5) | ((r < 0) << 4);
+        if (kind != 7) setA(r);
+        return;
+      }
+      case 4: r = a & v; f = ((r == 0) << 7) | 0x20; break;
+      case 5: r = a ^ v; f = (r == 0) << 7; break;
+      default: r = a | v; f = (r == 0) << 7; break;
+    }
+    setA(r);
+  }
+  __device__ __forceinline__ bool cond(int cc) const {
+    int bit = (cc & 2) ? ((f >> 4) & 1) : ((f >> 7) & 1);
+    return (cc & 1) ? bit : !bit;
+  }
+};
+
+template <int MBC>
+struct Emu {
+  // addressing
+  uint8_t* mem;           // env's 64 KiB address space (env-major)
+  uint32_t S;             // SoA row stride of the scalar fields
+  const uint32_t* pre_s;  // shared memory: pre-decoded rom[0 .. pre_s_words)
+  const uint32_t* pre_g;  // global pre-decoded ROM
+  const uint8_t* boot_s;  // shared memory: boot ROM
+  const uint8_t* rom_g;   // global ROM bytes
+  int32_t* cart_state;    // &st.cart_state[env]
+  uint8_t* cart_ram;      // env's cartridge RAM (env-major)
+  uint8_t* serial;        // env's serial capture buffer (env-major)
+  int32_t* i32;           // &st.i32[env]
+  uint8_t* u8s;           // &st.u8s[env]
+  uint8_t* latch;         // st.latch
+  int rom_bank_count, rom_bank_mask, ram_bank_count;
+  int pre_s_words;
+  int is_env0;
+  // CPU (the interpreter loop's registers, copied in around slow paths)
+  uint32_t bcde, hlxa;   // B C D E | H L - A, high byte first
+  int f, pc, sp;
+  int ime, ime_delay, halted;
+  int trap;
+  // cached IO ports (values of mem[FFxx]); stat/div_b/prev_in/stat_prev are
+  // exact only while lazy == 0
+  int joyp, div_b, tima, tma, tac, iflag, lcdc, stat, ly_b, lyc, wy, ie;
+  // timer
+  int div, rl_pending, rl_delay, prev_in;
+  // PPU
+  int scan, ly, wl, stat_prev;
+  // cart
+  int ram_en, bank_lo, bank_hi, ram_bank, bank_mode, bootrom, rtc_sel, rtc_latch;
+  int bank0_off, bankN_off;   // ROM byte offset of a bank region; -1 when out of range
+  int win_lo, win_len;        // fetch window: pc in [win_lo, win_lo + win_len) reads pre_s[pc]
+  int cram_off;               // cart RAM offset of the bank at A000-BFFF; -1 when such
+                              // accesses need the full path (disabled, absent, RTC)
+  int rtc_sub, rtc_s, rtc_m, rtc_h, rtc_dl, rtc_dh;
+  // step
+  int frames_done, release, action;
+  int cycle_frame, cyc_run, ninstr;
+  // lazy state
+  int lazy, ev, clk, next_ev, stat_hi, lcd_on, rtc_run, lcdc_before;
 
   // ---- memory -------------------------------------------------------------
   __device__ __forceinline__ uint8_t& M(int a) const { return mem[a]; }
@@ -228,6 +268,26 @@ struct Emu {
     else { b0 %= cnt; bn %= cnt; }
     bank0_off = b0 < cnt ? b0 * ROM_BANK : -1;
     bankN_off = bn < cnt ? bn * ROM_BANK - ROM_BANK : -1;
+    // Shared memory holds the pre-decoded words of ROM offsets [0, pre_s_words).
+    // With bank 0 at offset 0 the bank-0 region fetches from it (minus the
+    // boot ROM overlay and the last two bytes, whose instruction could reach
+    // into bank N); with bank 1 also mapped the window spans both regions.
+    win_lo = bootrom ? 0x100 : 0;
+    int hi = 0;
+    if (bank0_off == 0) hi = (bankN_off == 0 && pre_s_words >= 0x8000) ? 0x7FFE : 0x3FFE;
+    win_len = hi > win_lo ? hi - win_lo : 0;
+    // A000-BFFF as plain bytes when it maps a whole bank of cart RAM
+    // (ram_index / cart_read with RAM enabled and no RTC register selected)
+    cram_off = -1;
+    if (ram_bank_count > 0 && ram_en != 0) {
+      const int sel = rtc_sel & 0x0F;
+      if (!(MBC == MBC_MBC3 && sel >= 0x08 && sel <= 0x0C)) {
+        int rb = 0;
+        if (MBC == MBC_MBC1) { if (bank_mode & 1) rb = ram_bank & 3; }
+        else if (MBC == MBC_MBC3) rb = ram_bank & 3;
+        cram_off = (rb % ram_bank_count) * RAM_BANK;
+      }
+    }
   }
 
   __device__ __forceinline__ int rom_read(int a) const {
@@ -237,33 +297,48 @@ struct Emu {
     return __ldg(rom_g + off + a);
   }
 
-  // STAT low bits / stat_prev / DIV as functions of the state at the last
-  // sync plus clk (lazy mode)
-  __device__ __forceinline__ int ppu_mode_at(int sc) const {
-    return ly >= SCREEN_H ? 1 : sc < 80 ? 2 : sc < 250 ? 3 : 0;
+  // STAT low bits / stat_prev / LY / DIV / TIMA as functions of the state at
+  // the last sync plus clk (lazy mode). A lazy period may cross scanlines
+  // (never VBlank entry or the wrap to line 0) and TIMA edges (never an
+  // overflow), see delazify().
+  __device__ __forceinline__ static int mode_at(int line, int sc) {
+    return line >= SCREEN_H ? 1 : sc < 80 ? 2 : sc < 250 ? 3 : 0;
   }
+  __device__ __forceinline__ int ppu_mode_at(int sc) const { return mode_at(ly, sc); }
   __device__ __forceinline__ static int prev_bits(int mode, int coinc) {
     return (mode == 0) | ((mode == 1) << 1) | ((mode == 2) << 2) | (coinc << 3);
   }
   __device__ __forceinline__ int stat_now() const {
     if (!lazy) return stat;
-    return stat_hi | ((ly == lyc) << 2) | (lcd_on ? ppu_mode_at(scan + clk) : 0);
+    if (!lcd_on) return stat_hi | ((ly == lyc) << 2);
+    const int t = scan + clk, n = t / CYCLES_PER_LINE, line = ly + n;
+    return stat_hi | ((line == lyc) << 2) | mode_at(line, t - n * CYCLES_PER_LINE);
+  }
+  __device__ __forceinline__ int ly_b_now() const {
+    if (!lazy || !lcd_on) return ly_b;
+    const int n = (scan + clk) / CYCLES_PER_LINE;
+    return n ? ly + n : ly_b;
   }
   __device__ __forceinline__ int div_byte_now() const {
     return lazy ? (((div + clk) >> 8) & 0xFF) : div_b;
+  }
+  __device__ __forceinline__ int tima_now() const {
+    if (!lazy || !(tac & 4) || rl_pending) return tima;
+    const int sh = div_bit(tac) + 1;
+    return tima + (((div & ((1 << sh) - 1)) + clk) >> sh);
   }
 
   __device__ __forceinline__ int io_read(int a) const {
     switch (a & 0xFF) {
       case 0x00: return joyp;
       case 0x04: return div_byte_now();
-      case 0x05: return tima;
+      case 0x05: return tima_now();
       case 0x06: return tma;
       case 0x07: return tac;
       case 0x0F: return iflag;
       case 0x40: return lcdc;
       case 0x41: return stat_now();
-      case 0x44: return ly_b;
+      case 0x44: return ly_b_now();
       case 0x45: return lyc;
       case 0x4A: return wy;
       case 0xFF: return ie;
@@ -336,11 +411,19 @@ struct Emu {
     rl_pending = 0;
     rl_delay = 0;
   }
-  // the reference's timer_tick, exact
+  // the reference's timer_tick, exact. Without a pending reload and with no
+  // overflow inside `cycles`, its edge loop only counts TIMA edges, which is
+  // done in closed form.
   __device__ void timer_tick(int cycles) {
     if (cycles <= 0) return;
-    if (!(tac & 4) && !rl_pending) {
+    int edges = 0;
+    if (!rl_pending && (tac & 4)) {
+      const int sh = div_bit(tac) + 1;
+      edges = ((div & ((1 << sh) - 1)) + cycles) >> sh;
+    }
+    if (!rl_pending && tima + edges <= 0xFF) {
       div = (div + cycles) & 0xFFFF;
+      tima += edges;
     } else {
       int remaining = cycles;
       int d = div & 0xFFFF;
@@ -366,13 +449,16 @@ struct Emu {
     div_b = (div >> 8) & 0xFF;
     prev_in = timer_in(div, tac);
   }
-  // cycles from now until timer_tick would do more than advance DIV
+  // cycles from now until timer_tick does more than advance DIV and count
+  // TIMA edges: the overflow edge, or while a reload is pending the reload
+  // and the next edge
   __device__ __forceinline__ int timer_event() const {
     int t = INT_MAX;
     if (rl_pending) t = rl_delay;
     if (tac & 4) {
       int period = 1 << (div_bit(tac) + 1);
       int e = period - (div & (period - 1));
+      if (!rl_pending) e += (0xFF - tima) * period;
       t = e < t ? e : t;
     }
     return t;
@@ -460,8 +546,25 @@ struct Emu {
   // Advance every lazily tracked counter by q event-free cycles.
   __device__ void apply_quiet(int q) {
     if (q <= 0) return;
-    timer_tick(q);  // no edge or reload inside q (q < next_ev)
-    if (lcd_on) scan += q;
+    timer_tick(q);  // no overflow or reload inside q (q < next_ev)
+    if (lcd_on) {
+      // whole scanlines inside q: none of them enters VBlank or wraps, and
+      // with the STAT interrupt enables clear each one only moves LY, LY's
+      // register and the window line (ppu_advance's per-line body)
+      const int t = scan + q;
+      if (t >= CYCLES_PER_LINE) {
+        const int n = t / CYCLES_PER_LINE;
+        scan = t - n * CYCLES_PER_LINE;
+        if (lcdc & 0x20) {
+          const int lo = ly > wy ? ly : wy, hi = ly + n < SCREEN_H ? ly + n : SCREEN_H;
+          if (hi > lo) wl += hi - lo;
+        }
+        ly += n;
+        ly_b = ly;
+      } else {
+        scan = t;
+      }
+    }
     if (MBC == MBC_MBC3) rtc_sub += q & rtc_run;
     cycle_frame += q;
     cyc_run += q;
@@ -489,7 +592,14 @@ struct Emu {
     lcd_on = (lcdc & 0x80) != 0;
     rtc_run = (MBC == MBC_MBC3 && !(rtc_dh & 0x40) && rtc_sub >= 0) ? -1 : 0;
     int t = timer_event();
-    if (lcd_on) { int p = CYCLES_PER_LINE - scan; t = p < t ? p : t; }
+    if (lcd_on) {
+      int p = CYCLES_PER_LINE - scan;  // next scanline
+      // Line changes only need the exact path when they can raise a STAT
+      // interrupt, enter VBlank, wrap to line 0 or latch env 0's registers.
+      if (!is_env0 && !(stat_hi & 0x78))
+        p += ((ly < SCREEN_H ? SCREEN_H : LINES_PER_FRAME) - 1 - ly) * CYCLES_PER_LINE;
+      t = p < t ? p : t;
+    }
     { int fr = CYCLES_PER_FRAME - cycle_frame; t = fr < t ? fr : t; }
     if (MBC == MBC_MBC3 && rtc_run) { int r = RTC_CPS - rtc_sub; t = r < t ? r : t; }
     next_ev = t;
@@ -541,7 +651,7 @@ struct Emu {
         }
         return;
       case 0x50:
-        if (val != 0) bootrom = 0;
+        if (val != 0) { bootrom = 0; update_banks(); }
         return;
       case 0x04: case 0x05: case 0x06: case 0x07: {
         sync_all();
@@ -578,19 +688,24 @@ struct Emu {
       }
       case 0xFF: ie = v8 & 0x1F; ev |= EV_IRQ; return;
       case 0x40:
+        sync_all();  // lines so far ran under the old LCDC
         if (!(ev & EV_LCDC)) lcdc_before = lcdc;
         lcdc = v8;
         ev |= EV_LCDC;
         return;
-      case 0x41: stat = v8; stat_hi = v8 & 0xF8; return;
-      case 0x44: ly_b = v8; ev |= EV_PPU; return;
+      case 0x41:
+        sync_all();  // interrupt enables change which line changes matter
+        stat = v8; stat_hi = v8 & 0xF8;
+        ev |= EV_PPU;
+        return;
+      case 0x44: sync_all(); ly_b = v8; ev |= EV_PPU; return;
       case 0x45:
         // stat_prev of the last refresh was computed with the old LYC
         sync_all();
         lyc = v8;
         ev |= EV_PPU;
         return;
-      case 0x4A: wy = v8; return;
+      case 0x4A: sync_all(); wy = v8; ev |= EV_PPU; return;  // the window line count uses WY
       default: M(a) = (uint8_t)v8; return;
     }
   }
@@ -637,6 +752,7 @@ struct Emu {
             rtc_latch = 1;
           }
         }
+        update_banks();
       }
       return;
     }
@@ -647,27 +763,6 @@ struct Emu {
     const int a = addr & 0xFFFF;
     if (((a >> 13) | 2) == 6) { M(a) = (uint8_t)val; return; }  // VRAM, WRAM
     write8_slow(a, val);
-  }
-
-  // ---- ALU (alu.py), branch-free over the 8 kinds ----------------------------
-  __device__ __forceinline__ void alu(int kind, int v) {
-    const int a = A();
-    const int cin = (kind == 1 || kind == 3) ? ((f >> 4) & 1) : 0;
-    const bool sub = kind == 2 || kind == 3 || kind == 7;
-    const int lo = sub ? (a & 0xF) - (v & 0xF) - cin : (a & 0xF) + (v & 0xF) + cin;
-    const int full = sub ? a - v - cin : a + v + cin;
-    const int h = sub ? lo < 0 : lo > 0xF;
-    const int c = sub ? full < 0 : full > 0xFF;
-    const bool logic = kind >= 4 && kind <= 6;
-    const int lres = kind == 4 ? (a & v) : kind == 5 ? (a ^ v) : (a | v);
-    const int res = (logic ? lres : full) & 0xFF;
-    const int fl = logic ? (kind == 4 ? 0x20 : 0) : ((sub << 6) | (h << 5) | (c << 4));
-    f = ((res == 0) << 7) | fl;
-    if (kind != 7) setA(res);
-  }
-  __device__ __forceinline__ bool cond(int cc) const {
-    int bit = (cc & 2) ? ((f >> 4) & 1) : ((f >> 7) & 1);
-    return (cc & 1) ? bit : !bit;
   }
 
   // interrupt service (:1502-1604): IME off, IF bit cleared, PC pushed
@@ -740,7 +835,11 @@ struct Emu {
     if ((ie & iflag & 0x1F) == 0 && cycle_frame < CYCLES_PER_FRAME) {
       int kmax = (CYCLES_PER_FRAME - cycle_frame + 3) >> 2;  // iteration that ends the frame
       if (lcdc & 0x80) {
-        int kl = (CYCLES_PER_LINE - scan + 3) >> 2;          // iteration that crosses a line
+        // iteration that crosses a line the exact path must see (as in delazify)
+        int to_line = CYCLES_PER_LINE - scan;
+        if (!is_env0 && !(stat & 0x78))
+          to_line += ((ly < SCREEN_H ? SCREEN_H : LINES_PER_FRAME) - 1 - ly) * CYCLES_PER_LINE;
+        int kl = (to_line + 3) >> 2;
         kmax = kl < kmax ? kl : kmax;
       }
       if ((tac & 4) || rl_pending) {
@@ -787,6 +886,40 @@ struct Emu {
       frames_done++;
       if (frames_done >= frames_to_run) break;
     }
+  }
+
+  // ---- out-of-line entry points of the interpreter loop ----------------------
+  // They take `this` by address, so the cold state stays in local memory and
+  // out of the loop's registers. Each is reached once per event, slow memory
+  // access or fetch outside the window, not once per instruction.
+  __device__ __noinline__ int read_slow(int a) { return read8(a); }
+  __device__ __noinline__ void write_slow(int a, int v) { write8_slow(a & 0xFFFF, v); }
+  // instruction bytes through the memory map (boot ROM overlay, RAM, bank
+  // ends, banks outside the window)
+  __device__ __noinline__ uint32_t fetch_slow(int at, const uint8_t* dec) {
+    const int op = read8(at), b1 = read8((at + 1) & 0xFFFF), b2 = read8((at + 2) & 0xFFFF);
+    uint32_t e = dec[op];
+    if (op == 0xCB && (b1 & 7) == 6) e |= RD_HL << 5;
+    return (uint32_t)op | ((uint32_t)b1 << 8) | ((uint32_t)b2 << 16) | (e << 24);
+  }
+  // the exact tail of one instruction plus the halted iterations it leads
+  // into; true when the launch's frames are done
+  __device__ __noinline__ bool tail_slow(int cyc, int opcode, int pc_before, int frames_to_run) {
+    slow_post(cyc, opcode, pc_before, frames_to_run);
+    while (halted && frames_done < frames_to_run) {
+      materialize();
+      halted_step(frames_to_run);
+      delazify();
+    }
+    return frames_done >= frames_to_run;
+  }
+  // unimplemented opcode (misc.py:42-56)
+  __device__ __noinline__ void trap_op(int at, int op) {
+    trap = 1;
+    ev |= EV_TRAP;
+    i32[(size_t)F_TRAP_PC * S] = at & 0xFFFF;
+    i32[(size_t)F_TRAP_OPCODE * S] = op & 0xFF;
+    i32[(size_t)F_TRAP_KIND * S] = 1;
   }
 };
 
@@ -908,21 +1041,54 @@ __global__ void __launch_bounds__(MAXT, 1)
     while (s.halted && s.frames_done < frames_to_run) s.halted_step(frames_to_run);
     run = s.frames_done < frames_to_run;
   }
+
+  // ---- interpreter loop: registers in h, cold state in s ----
+  Hot h;
+  h.bcde = s.bcde; h.hlxa = s.hlxa; h.f = s.f; h.pc = s.pc; h.sp = s.sp;
+  h.clk = 0;
+  h.next_ev = INT_MIN;  // EV_FIRST: the first instruction takes the exact tail
+  int ninstr = 0;
+  int win_lo = s.win_lo, win_len = s.win_len, bankN_off = s.bankN_off, cram_off = s.cram_off;
+  uint8_t* const mem = s.mem;
+  uint8_t* const cram = s.cart_ram;
+  auto save = [&]() {
+    s.bcde = h.bcde; s.hlxa = h.hlxa; s.f = h.f; s.pc = h.pc; s.sp = h.sp; s.clk = h.clk;
+  };
+  auto load = [&]() {
+    h.bcde = s.bcde; h.hlxa = s.hlxa; h.f = s.f; h.pc = s.pc; h.sp = s.sp; h.clk = s.clk;
+    h.next_ev = s.next_ev;
+    win_lo = s.win_lo; win_len = s.win_len; bankN_off = s.bankN_off; cram_off = s.cram_off;
+  };
+  // VRAM, WRAM and HRAM are plain bytes of the env's address space
+  auto plain = [](int a) { return ((a >> 13) | 2) == 6 || (unsigned)(a - 0xFF80) < 0x7Fu; };
+  auto rd = [&](int a) -> int {
+    if (plain(a)) return mem[a];
+    if ((unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0) return cram[cram_off + a - 0xA000];
+    s.clk = h.clk;  // lazy DIV/TIMA/STAT/LY reads need the clock
+    return s.read_slow(a);
+  };
+  auto wr = [&](int a, int v) {
+    if (plain(a)) { mem[a] = (uint8_t)v; return; }
+    if ((unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0) { cram[cram_off + a - 0xA000] = (uint8_t)v; return; }
+    s.clk = h.clk;
+    s.write_slow(a, v);  // ev is 0 here unless an earlier write of this instruction set it
+    h.clk = s.clk;       // a timing write syncs (clk = 0) and sets ev
+    if (s.ev) h.next_ev = INT_MIN;
+    win_lo = s.win_lo; win_len = s.win_len; bankN_off = s.bankN_off; cram_off = s.cram_off;
+  };
+
   while (run) {
     // ---- fetch + decode ----
-    const int pc = s.pc;
+    const int pc = h.pc;
     uint32_t w;
-    {
-      const int off = (pc & 0x4000) ? s.bankN_off : s.bank0_off;
-      if (pc < 0x8000 && (pc & 0x3FFF) < 0x3FFE && off >= 0 && (pc >= 0x100 || !s.bootrom)) {
-        const int idx = off + pc;
-        w = idx < s.pre_s_words ? s.pre_s[idx] : __ldg(s.pre_g + idx);
-      } else {
-        const int op = s.read8(pc), b1 = s.read8(pc + 1), b2 = s.read8(pc + 2);
-        uint32_t e = dec_s[op];
-        if (op == 0xCB && (b1 & 7) == 6) e |= RD_HL << 5;
-        w = (uint32_t)op | ((uint32_t)b1 << 8) | ((uint32_t)b2 << 16) | (e << 24);
-      }
+    if ((unsigned)(pc - win_lo) < (unsigned)win_len) {
+      w = pre_s[pc];
+    } else if ((unsigned)(pc - 0x4000) < 0x3FFEu && bankN_off >= 0) {
+      const int idx = pc + bankN_off;
+      w = idx < pre_s_words ? pre_s[idx] : __ldg(pre_g + idx);
+    } else {
+      s.clk = h.clk;
+      w = s.fetch_slow(pc, dec_s);
     }
     const int opcode = w & 0xFF;
     const int imm8 = (w >> 8) & 0xFF;
@@ -934,16 +1100,16 @@ __global__ void __launch_bounds__(MAXT, 1)
     if (rmode != RD_NONE) {
       int ra;
       switch (rmode) {
-        case RD_HL: ra = s.HL(); break;
-        case RD_BC: ra = s.BC(); break;
-        case RD_DE: ra = s.DE(); break;
+        case RD_HL: ra = h.HL(); break;
+        case RD_BC: ra = h.BC(); break;
+        case RD_DE: ra = h.DE(); break;
         case RD_A16: ra = imm16; break;
         case RD_FF_N: ra = 0xFF00 | imm8; break;
-        case RD_FF_C: ra = 0xFF00 | s.C_(); break;
-        default: ra = s.sp; break;
+        case RD_FF_C: ra = 0xFF00 | h.C_(); break;
+        default: ra = h.sp; break;
       }
-      v1 = s.read8(ra);
-      if (rmode == RD_SP) v2 = s.read8((ra + 1) & 0xFFFF);
+      v1 = rd(ra);
+      if (rmode == RD_SP) v2 = rd((ra + 1) & 0xFFFF);
     }
     // ---- execute ----
     int npc = pc + 1;
@@ -951,25 +1117,25 @@ __global__ void __launch_bounds__(MAXT, 1)
     int nw = 0, wa0 = 0, wv0 = 0, wa1 = 0, wv1 = 0;
     const int y = (opcode >> 3) & 7, z = opcode & 7;
     switch (fam) {
-      case FM_LDRR: s.setr(y, s.getr(z)); break;  // includes NOP (LD B,B form)
-      case FM_LD16: s.setp((opcode >> 4) & 3, imm16); npc = pc + 3; cyc = 12; break;
+      case FM_LDRR: h.setr(y, h.getr(z)); break;  // includes NOP (LD B,B form)
+      case FM_LD16: h.setp((opcode >> 4) & 3, imm16); npc = pc + 3; cyc = 12; break;
       case FM_ST_A:
-        nw = 1; wv0 = s.A();
+        nw = 1; wv0 = h.A();
         if (opcode < 0x40) {
           const int p = (opcode >> 4) & 3;  // 0 BC, 1 DE, 2 HL+, 3 HL-
-          const int ad = p == 0 ? s.BC() : p == 1 ? s.DE() : s.HL();
+          const int ad = p == 0 ? h.BC() : p == 1 ? h.DE() : h.HL();
           wa0 = ad;
-          if (p >= 2) s.setHL(p == 2 ? ad + 1 : ad - 1);
+          if (p >= 2) h.setHL(p == 2 ? ad + 1 : ad - 1);
           cyc = 8;
         } else if (opcode == 0xE0) { wa0 = 0xFF00 | imm8; npc = pc + 2; cyc = 12; }
-        else if (opcode == 0xE2) { wa0 = 0xFF00 | s.C_(); cyc = 8; }
+        else if (opcode == 0xE2) { wa0 = 0xFF00 | h.C_(); cyc = 8; }
         else { wa0 = imm16; npc = pc + 3; cyc = 16; }
         break;
       case FM_LD_A:
-        s.setA(v1);
+        h.setA(v1);
         if (opcode < 0x40) {
           const int p = (opcode >> 4) & 3;
-          if (p >= 2) { const int hl = s.HL(); s.setHL(p == 2 ? hl + 1 : hl - 1); }
+          if (p >= 2) { const int hl = h.HL(); h.setHL(p == 2 ? hl + 1 : hl - 1); }
           cyc = 8;
         } else if (opcode == 0xF0) { npc = pc + 2; cyc = 12; }
         else if (opcode == 0xF2) { cyc = 8; }
@@ -977,84 +1143,84 @@ __global__ void __launch_bounds__(MAXT, 1)
         break;
       case FM_INCDEC16: {
         const int p = (opcode >> 4) & 3;
-        s.setp(p, s.getp(p) + ((opcode & 8) ? -1 : 1));
+        h.setp(p, h.getp(p) + ((opcode & 8) ? -1 : 1));
         cyc = 8; break;
       }
       case FM_INCDEC8: {
         const int dec1 = z & 1;
-        const int old = s.getr(y), v = (dec1 ? old - 1 : old + 1) & 0xFF;
-        s.setr(y, v);
-        s.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (s.f >> 4) & 1);
+        const int old = h.getr(y), v = (dec1 ? old - 1 : old + 1) & 0xFF;
+        h.setr(y, v);
+        h.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (h.f >> 4) & 1);
         break;
       }
       case FM_INCDEC_HL: {
         const int old = v1, dec1 = z & 1;
         const int v = (dec1 ? old - 1 : old + 1) & 0xFF;
-        s.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (s.f >> 4) & 1);
-        nw = 1; wa0 = s.HL(); wv0 = v;
+        h.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (h.f >> 4) & 1);
+        nw = 1; wa0 = h.HL(); wv0 = v;
         cyc = 12; break;
       }
-      case FM_LD8_IMM: s.setr(y, imm8); npc = pc + 2; cyc = 8; break;
-      case FM_ST_HL_IMM: nw = 1; wa0 = s.HL(); wv0 = imm8; npc = pc + 2; cyc = 12; break;
+      case FM_LD8_IMM: h.setr(y, imm8); npc = pc + 2; cyc = 8; break;
+      case FM_ST_HL_IMM: nw = 1; wa0 = h.HL(); wv0 = imm8; npc = pc + 2; cyc = 12; break;
       case FM_ROTA: {
-        const int a = s.A(), oc = (s.f >> 4) & 1;
+        const int a = h.A(), oc = (h.f >> 4) & 1;
         const int right = y & 1, thru = y >> 1;
         const int c = right ? (a & 1) : ((a >> 7) & 1);
         const int in = thru ? oc : c;
         const int r = right ? ((a >> 1) | (in << 7)) : (((a << 1) & 0xFF) | in);
-        s.setA(r); s.f = FLAGS(0, 0, 0, c);
+        h.setA(r); h.f = FLAGS(0, 0, 0, c);
         break;
       }
       case FM_ST_SP16:
-        nw = 2; wa0 = imm16; wv0 = s.sp & 0xFF; wa1 = (imm16 + 1) & 0xFFFF; wv1 = (s.sp >> 8) & 0xFF;
+        nw = 2; wa0 = imm16; wv0 = h.sp & 0xFF; wa1 = (imm16 + 1) & 0xFFFF; wv1 = (h.sp >> 8) & 0xFF;
         npc = pc + 3; cyc = 20; break;
       case FM_ADDHL: {
-        const int hl = s.HL(), rr = s.getp((opcode >> 4) & 3), sum = hl + rr;
-        s.f = FLAGS((s.f >> 7) & 1, 0, ((hl & 0xFFF) + (rr & 0xFFF)) > 0xFFF, sum > 0xFFFF);
-        s.setHL(sum);
+        const int hl = h.HL(), rr = h.getp((opcode >> 4) & 3), sum = hl + rr;
+        h.f = FLAGS((h.f >> 7) & 1, 0, ((hl & 0xFFF) + (rr & 0xFFF)) > 0xFFF, sum > 0xFFFF);
+        h.setHL(sum);
         cyc = 8; break;
       }
       case FM_JR: {
-        const bool t = opcode == 0x18 || s.cond(y);
+        const bool t = opcode == 0x18 || h.cond(y);
         npc = pc + 2 + (t ? sign8(imm8) : 0);
         cyc = t ? 12 : 8;
         break;
       }
       case FM_DAA: {
-        int a = s.A(), n = (s.f >> 6) & 1, h = (s.f >> 5) & 1, c = (s.f >> 4) & 1, adj = 0, carry = c;
+        int a = h.A(), n = (h.f >> 6) & 1, hf = (h.f >> 5) & 1, c = (h.f >> 4) & 1, adj = 0, carry = c;
         if (!n) {
-          if (h || (a & 0xF) > 9) adj |= 0x06;
+          if (hf || (a & 0xF) > 9) adj |= 0x06;
           if (c || a > 0x99) { adj |= 0x60; carry = 1; }
           a = (a + adj) & 0xFF;
         } else {
-          if (h) adj |= 0x06;
+          if (hf) adj |= 0x06;
           if (c) adj |= 0x60;
           a = (a - adj) & 0xFF;
         }
-        s.f = FLAGS(a == 0, n, 0, carry); s.setA(a);
+        h.f = FLAGS(a == 0, n, 0, carry); h.setA(a);
         break;
       }
       case FM_FLAGOP: {  // CPL (y=5), SCF (y=6), CCF (y=7)
-        const int zf = (s.f >> 7) & 1, cf = (s.f >> 4) & 1;
-        if (y == 5) { s.setA(s.A() ^ 0xFF); s.f = FLAGS(zf, 1, 1, cf); }
-        else s.f = FLAGS(zf, 0, 0, y == 6 ? 1 : !cf);
+        const int zf = (h.f >> 7) & 1, cf = (h.f >> 4) & 1;
+        if (y == 5) { h.setA(h.A() ^ 0xFF); h.f = FLAGS(zf, 1, 1, cf); }
+        else h.f = FLAGS(zf, 0, 0, y == 6 ? 1 : !cf);
         break;
       }
-      case FM_LDR_HL: s.setr(y, v1); cyc = 8; break;
-      case FM_STHL_R: nw = 1; wa0 = s.HL(); wv0 = s.getr(z); cyc = 8; break;
-      case FM_HALT: s.halted = 1; s.ev |= EV_HALT; break;
-      case FM_ALU_R: s.alu(y, s.getr(z)); break;
+      case FM_LDR_HL: h.setr(y, v1); cyc = 8; break;
+      case FM_STHL_R: nw = 1; wa0 = h.HL(); wv0 = h.getr(z); cyc = 8; break;
+      case FM_HALT: s.halted = 1; s.ev |= EV_HALT; h.next_ev = INT_MIN; break;
+      case FM_ALU_R: h.alu(y, h.getr(z)); break;
       case FM_ALU_V: {
         const bool hl = rmode == RD_HL;
-        s.alu(y, hl ? v1 : imm8);
+        h.alu(y, hl ? v1 : imm8);
         npc = pc + (hl ? 1 : 2);
         cyc = 8; break;
       }
       case FM_RET:
-        if (opcode == 0xC9 || opcode == 0xD9 || s.cond(y)) {
+        if (opcode == 0xC9 || opcode == 0xD9 || h.cond(y)) {
           npc = v1 | (v2 << 8);
-          s.sp = (s.sp + 2) & 0xFFFF;
-          if (opcode == 0xD9) { s.ime = 1; s.ime_delay = 0; s.ev |= EV_IRQ; }
+          h.sp = (h.sp + 2) & 0xFFFF;
+          if (opcode == 0xD9) { s.ime = 1; s.ime_delay = 0; s.ev |= EV_IRQ; h.next_ev = INT_MIN; }
           cyc = (opcode & 1) ? 16 : 20;
         } else {
           cyc = 8;
@@ -1062,24 +1228,24 @@ __global__ void __launch_bounds__(MAXT, 1)
         break;
       case FM_POP: {
         const int p = (opcode >> 4) & 3;
-        if (p == 3) { s.setA(v2); s.f = v1 & 0xF0; }
-        else s.setp(p, v1 | (v2 << 8));
-        s.sp = (s.sp + 2) & 0xFFFF;
+        if (p == 3) { h.setA(v2); h.f = v1 & 0xF0; }
+        else h.setp(p, v1 | (v2 << 8));
+        h.sp = (h.sp + 2) & 0xFFFF;
         cyc = 12; break;
       }
       case FM_JP:
-        if (opcode == 0xE9) { npc = s.HL(); break; }
+        if (opcode == 0xE9) { npc = h.HL(); break; }
         {
-          const bool t = opcode == 0xC3 || s.cond(y);
+          const bool t = opcode == 0xC3 || h.cond(y);
           npc = t ? imm16 : pc + 3;
           cyc = t ? 16 : 12;
         }
         break;
       case FM_CALL:
-        if (opcode == 0xCD || s.cond(y)) {
+        if (opcode == 0xCD || h.cond(y)) {
           const int ret = (pc + 3) & 0xFFFF;
-          nw = 2; wa0 = (s.sp - 1) & 0xFFFF; wv0 = ret >> 8; wa1 = (s.sp - 2) & 0xFFFF; wv1 = ret & 0xFF;
-          s.sp = (s.sp - 2) & 0xFFFF;
+          nw = 2; wa0 = (h.sp - 1) & 0xFFFF; wv0 = ret >> 8; wa1 = (h.sp - 2) & 0xFFFF; wv1 = ret & 0xFF;
+          h.sp = (h.sp - 2) & 0xFFFF;
           npc = imm16; cyc = 24;
         } else {
           npc = pc + 3; cyc = 12;
@@ -1087,88 +1253,96 @@ __global__ void __launch_bounds__(MAXT, 1)
         break;
       case FM_PUSH: {
         const int p = (opcode >> 4) & 3;
-        const int v = p == 3 ? ((s.A() << 8) | (s.f & 0xF0)) : s.getp(p);
-        nw = 2; wa0 = (s.sp - 1) & 0xFFFF; wv0 = v >> 8; wa1 = (s.sp - 2) & 0xFFFF; wv1 = v & 0xFF;
-        s.sp = (s.sp - 2) & 0xFFFF;
+        const int v = p == 3 ? ((h.A() << 8) | (h.f & 0xF0)) : h.getp(p);
+        nw = 2; wa0 = (h.sp - 1) & 0xFFFF; wv0 = v >> 8; wa1 = (h.sp - 2) & 0xFFFF; wv1 = v & 0xFF;
+        h.sp = (h.sp - 2) & 0xFFFF;
         cyc = 16; break;
       }
       case FM_RST: {
         const int ret = (pc + 1) & 0xFFFF;
-        nw = 2; wa0 = (s.sp - 1) & 0xFFFF; wv0 = ret >> 8; wa1 = (s.sp - 2) & 0xFFFF; wv1 = ret & 0xFF;
-        s.sp = (s.sp - 2) & 0xFFFF;
+        nw = 2; wa0 = (h.sp - 1) & 0xFFFF; wv0 = ret >> 8; wa1 = (h.sp - 2) & 0xFFFF; wv1 = ret & 0xFF;
+        h.sp = (h.sp - 2) & 0xFFFF;
         npc = opcode & 0x38; cyc = 16; break;
       }
       case FM_CB: {
-        // bitops.py: all 256 CB ops, branch-free over the group
+        // bitops.py: RLC RRC RL RR SLA SRA SWAP SRL, BIT, RES, SET
         const int cb = imm8, cz = cb & 7, cy = (cb >> 3) & 7, grp = cb >> 6;
         const bool hl = cz == 6;
-        const int v = hl ? v1 : s.getr(cz);
-        const int oc = (s.f >> 4) & 1;
-        const int right = cy & 1;
-        const int lin = cy == 0 ? (v >> 7) & 1 : cy == 2 ? oc : 0;
-        const int rin = cy == 1 ? (v & 1) << 7 : cy == 3 ? oc << 7 : cy == 5 ? (v & 0x80) : 0;
-        const int sh = cy == 6 ? (((v & 0xF) << 4) | (v >> 4)) : right ? ((v >> 1) | rin) : (((v << 1) & 0xFF) | lin);
-        const int shc = cy == 6 ? 0 : right ? (v & 1) : ((v >> 7) & 1);
-        const int mask = 1 << cy;
-        const int res = grp == 0 ? sh : grp == 2 ? (v & ~mask) : (v | mask);
-        if (grp == 0) s.f = FLAGS(res == 0, 0, 0, shc);
-        if (grp == 1) s.f = FLAGS((v & mask) == 0, 0, 1, oc);
+        const int v = hl ? v1 : h.getr(cz);
         npc = pc + 2;
-        if (grp == 1) { cyc = hl ? 12 : 8; break; }
-        if (hl) { nw = 1; wa0 = s.HL(); wv0 = res; cyc = 16; }
-        else { s.setr(cz, res); cyc = 8; }
+        if (grp == 1) {  // BIT: Z from the bit, H set, C kept
+          h.f = ((((v >> cy) & 1) ^ 1) << 7) | 0x20 | (h.f & 0x10);
+          cyc = hl ? 12 : 8;
+          break;
+        }
+        int res;
+        if (grp == 0) {
+          const int oc = (h.f >> 4) & 1;
+          int c;
+          switch (cy) {
+            case 0: c = v >> 7; res = ((v << 1) & 0xFF) | c; break;
+            case 1: c = v & 1; res = (v >> 1) | (c << 7); break;
+            case 2: c = v >> 7; res = ((v << 1) & 0xFF) | oc; break;
+            case 3: c = v & 1; res = (v >> 1) | (oc << 7); break;
+            case 4: c = v >> 7; res = (v << 1) & 0xFF; break;
+            case 5: c = v & 1; res = (v >> 1) | (v & 0x80); break;
+            case 6: c = 0; res = ((v & 0xF) << 4) | (v >> 4); break;
+            default: c = v & 1; res = v >> 1; break;
+          }
+          h.f = ((res == 0) << 7) | (c << 4);
+        } else {
+          res = grp == 2 ? (v & ~(1 << cy) & 0xFF) : (v | (1 << cy));
+        }
+        if (hl) { nw = 1; wa0 = h.HL(); wv0 = res; cyc = 16; }
+        else { h.setr(cz, res); cyc = 8; }
         break;
       }
       case FM_SPADD:
-        if (opcode == 0xF9) { s.sp = s.HL(); cyc = 8; break; }
+        if (opcode == 0xF9) { h.sp = h.HL(); cyc = 8; break; }
         {
-          const int ou = imm8, res = (s.sp + sign8(imm8)) & 0xFFFF;
-          s.f = FLAGS(0, 0, ((s.sp & 0xF) + (ou & 0xF)) > 0xF, ((s.sp & 0xFF) + ou) > 0xFF);
-          if (opcode == 0xE8) { s.sp = res; cyc = 16; }
-          else { s.setHL(res); cyc = 12; }
+          const int ou = imm8, res = (h.sp + sign8(imm8)) & 0xFFFF;
+          h.f = FLAGS(0, 0, ((h.sp & 0xF) + (ou & 0xF)) > 0xF, ((h.sp & 0xFF) + ou) > 0xFF);
+          if (opcode == 0xE8) { h.sp = res; cyc = 16; }
+          else { h.setHL(res); cyc = 12; }
           npc = pc + 2;
         }
         break;
       case FM_IME:
         s.ime_delay = 0;
-        if (opcode == 0xFB) { s.ime = 1; s.ev |= EV_IRQ; }
+        if (opcode == 0xFB) { s.ime = 1; s.ev |= EV_IRQ; h.next_ev = INT_MIN; }
         else s.ime = 0;
         break;
       default:  // FM_TRAP (misc.py:42-56)
-        s.trap = 1;
-        s.ev |= EV_TRAP;
-        st.i32[(size_t)F_TRAP_PC * S + env] = pc & 0xFFFF;
-        st.i32[(size_t)F_TRAP_OPCODE * S + env] = opcode & 0xFF;
-        st.i32[(size_t)F_TRAP_KIND * S + env] = 1;
+        s.trap_op(pc, opcode);
+        h.next_ev = INT_MIN;
         npc = pc;
         cyc = 0;
         break;
     }
-    s.pc = npc & 0xFFFF;
+    h.pc = npc & 0xFFFF;
     // ---- memory writes ----
     if (nw) {
-      s.write8(wa0, wv0);
-      if (nw == 2) s.write8(wa1, wv1);
+      wr(wa0, wv0);
+      if (nw == 2) wr(wa1, wv1);
     }
     // ---- tail ----
-    if (s.ev & EV_TRAP) break;
-    s.ninstr++;
-    s.clk += cyc;
-    if (s.clk >= s.next_ev || s.ev) {
-      s.slow_post(cyc, opcode, pc, frames_to_run);
-      while (s.halted && s.frames_done < frames_to_run) {
-        s.materialize();
-        s.halted_step(frames_to_run);
-        s.delazify();
-      }
-      if (s.frames_done >= frames_to_run) break;
+    h.clk += cyc;
+    ninstr++;
+    if (h.clk >= h.next_ev) {
+      if (s.trap) { ninstr--; break; }
+      save();
+      const bool done = s.tail_slow(cyc, opcode, pc, frames_to_run);
+      load();
+      if (done) break;
     }
   }
+  if (run) save();
+  s.ninstr = ninstr;
   s.sync_all();
 
   // ---- post-step body (post_step.py:11-102) ----
-  const int a = s.A(), b = s.getr(0), c = s.getr(1), d = s.getr(2);
-  const int e_ = s.getr(3), h = s.getr(4), l = s.getr(5);
+  const int a = s.hlxa & 0xFF, b = (s.bcde >> 24) & 0xFF, c = (s.bcde >> 16) & 0xFF, d = (s.bcde >> 8) & 0xFF;
+  const int e_ = s.bcde & 0xFF, hh = (s.hlxa >> 24) & 0xFF, l = (s.hlxa >> 16) & 0xFF;
   if (stage == STAGE_OBS || stage == STAGE_FULL) {
     float* o = st.obs + (size_t)env * OBS_DIM;
     int m[16];
@@ -1182,7 +1356,7 @@ __global__ void __launch_bounds__(MAXT, 1)
     q[0] = make_float4((float)(s.pc & 0xFFFF) / 65535.0f, (float)(s.sp & 0xFFFF) / 65535.0f,
                        (float)a / 255.0f, (float)(s.f & 0xFF) / 255.0f);
     q[1] = make_float4((float)b / 255.0f, (float)c / 255.0f, (float)d / 255.0f, (float)e_ / 255.0f);
-    q[2] = make_float4((float)h / 255.0f, (float)l / 255.0f, (float)m[0] / 255.0f, (float)m[1] / 255.0f);
+    q[2] = make_float4((float)hh / 255.0f, (float)l / 255.0f, (float)m[0] / 255.0f, (float)m[1] / 255.0f);
     q[3] = make_float4((float)m[2] / 255.0f, (float)m[3] / 255.0f, (float)m[4] / 255.0f, (float)m[5] / 255.0f);
     q[4] = make_float4((float)m[6] / 255.0f, (float)m[7] / 255.0f, (float)m[8] / 255.0f, (float)m[9] / 255.0f);
     q[5] = make_float4((float)m[10] / 255.0f, (float)m[11] / 255.0f, (float)m[12] / 255.0f, (float)m[13] / 255.0f);
@@ -1203,7 +1377,7 @@ __global__ void __launch_bounds__(MAXT, 1)
   int32_t* O = st.i32 + env;
   auto stv = [&](int fld, int v) { O[(size_t)fld * S] = v; };
   stv(F_PC, s.pc & 0xFFFF); stv(F_SP, s.sp & 0xFFFF);
-  stv(F_A, a); stv(F_B, b); stv(F_C, c); stv(F_D, d); stv(F_E, e_); stv(F_H, h); stv(F_L, l);
+  stv(F_A, a); stv(F_B, b); stv(F_C, c); stv(F_D, d); stv(F_E, e_); stv(F_H, hh); stv(F_L, l);
   stv(F_F, s.f & 0xF0);
   stv(F_CYCLE_IN_FRAME, s.cycle_frame);
   stv(F_TRAP_FLAG, s.trap);
