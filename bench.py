@@ -56,6 +56,12 @@ WORKLOAD = "config2: PPU on (LCDC=0xE3) random-opcode loop, 4096 envs/GPU, frame
 # every per-env field it owns, the action, the f32 obs vector). Instruction
 # RAM traffic is not counted, so this is a lower bound.
 STEP_STATE_BYTES = 2 * (27 * 4 + 2 * 8 + 3 + 20 * 4 + 12) + 4 + 32 * 4
+# dram__bytes_read.sum + dram__bytes_write.sum of one step-kernel launch on
+# this workload (4,096 envs), from an ncu --set full capture of
+# `bench.py --steps 3 --warmup 3 --no-cpu-baseline`. It includes the
+# emulated programs' RAM lines and the write-back of the L2 flush buffer
+# written just before the launch.
+STEP_KERNEL_DRAM_BYTES_4096 = 75.305728e6 + 345.320448e6
 
 
 def _peaks() -> dict:
@@ -170,6 +176,7 @@ def run_gbx(args) -> None:
     import torch
 
     from gbxcule_b200 import GbxVecCudaBackend, roms
+    from gbxcule_b200.multi import job_rate, rank_seed, reduce_run_stats
 
     ws, rank, local = _dist()
     dist = None
@@ -187,7 +194,7 @@ def run_gbx(args) -> None:
     n = ENVS_PER_GPU
     K, W = args.steps, args.warmup
     rom = roms.CONFIG_ROMS[CONFIG]()
-    rng = np.random.default_rng(0 + rank)
+    rng = np.random.default_rng(rank_seed(0, rank))  # this rank's own env slice
     acts_host = np.stack([roms.uniform_actions(rng, n, 9) for _ in range(W + 2 * K)])
     be = GbxVecCudaBackend(rom, num_envs=n, frames_per_step=FRAMES, release_after_frames=RELEASE,
                            render_pixels_packed=True, render_on_step=False, device=f"cuda:{local}")
@@ -241,13 +248,8 @@ def run_gbx(args) -> None:
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
 
-    t = torch.tensor([total_ms, e2e_ms, float(np.mean(step_ms))], dtype=torch.float64, device=dev)
-    c = torch.tensor([ninstr], dtype=torch.float64, device=dev)
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dist.all_reduce(c, op=dist.ReduceOp.SUM)
-    total_ms, e2e_ms, step_avg_ms = (float(x) for x in t.tolist())
-    ninstr = float(c.item())
+    (total_ms, e2e_ms, step_avg_ms), (ninstr,) = reduce_run_stats(
+        dist, dev, [total_ms, e2e_ms, float(np.mean(step_ms))], [ninstr])
     be.close()
     if dist:
         dist.barrier()
@@ -255,11 +257,10 @@ def run_gbx(args) -> None:
     if rank != 0:
         return
     total_envs = n * ws
-    value = total_envs * K / (total_ms / 1e3)
+    value = job_rate(n, ws, K, total_ms)
     peaks = _peaks()
     achieved = STEP_STATE_BYTES * n / (step_avg_ms / 1e3) / 1e9
-    prof = ROOT / "profiles" / "traffic.json"
-    traffic = json.loads(prof.read_text()).get("step_kernel_dram_bytes_per_launch") if prof.exists() else None
+    traffic = STEP_KERNEL_DRAM_BYTES_4096 * n / 4096
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
         "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -272,7 +273,7 @@ def run_gbx(args) -> None:
         # (the step kernel is bound by integer issue per emulated instruction)
         "emulated_instr_per_s": ninstr / (step_avg_ms * K / 1e3),
         "emulated_instr_per_env_step": ninstr / (total_envs * K),
-        "e2e": {"value": total_envs * K / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": 4 * n,
+        "e2e": {"value": job_rate(n, ws, K, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": 4 * n,
                 "d2h_bytes_per_step": 72 * 20 * n},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
