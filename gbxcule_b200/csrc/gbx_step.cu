@@ -152,15 +152,19 @@ struct Hot {
   __device__ __forceinline__ int BC() const { return bcde >> 16; }
   __device__ __forceinline__ int DE() const { return bcde & 0xFFFF; }
   __device__ __forceinline__ int C_() const { return (bcde >> 16) & 0xFF; }
-  // r8 index: 0 B, 1 C, 2 D, 3 E, 4 H, 5 L, 7 A (6 = (HL), never passed)
+  // r8 index: 0 B, 1 C, 2 D, 3 E, 4 H, 5 L, 7 A (6 = (HL), never passed).
+  // {bcde, hlxa} read as one 8-byte array puts register i at byte i ^ 3.
   __device__ __forceinline__ int getr(int i) const {
-    uint32_t w = (i & 4) ? hlxa : bcde;
-    return (w >> ((3 - (i & 3)) * 8)) & 0xFF;
+    return __byte_perm(bcde, hlxa, (i ^ 3) & 7) & 0xFF;
   }
-  __device__ __forceinline__ void setr(int i, int v) {
-    int sh = (3 - (i & 3)) * 8;
-    uint32_t m = ~(0xFFu << sh), val = (uint32_t)(v & 0xFF) << sh;
-    if (i & 4) hlxa = (hlxa & m) | val; else bcde = (bcde & m) | val;
+  __device__ __forceinline__ static uint32_t insert_byte(uint32_t w, int v, int pos) {
+    uint32_t r;
+    asm("bfi.b32 %0, %1, %2, %3, 8;" : "=r"(r) : "r"(v), "r"(w), "r"(pos));
+    return r;
+  }
+  __device__ __forceinline__ void setr(int i, int v) {  // v: low 8 bits are stored
+    const int pos = (~i & 3) << 3;
+    if (i & 4) hlxa = insert_byte(hlxa, v, pos); else bcde = insert_byte(bcde, v, pos);
   }
   // pair index: 0 BC, 1 DE, 2 HL, 3 SP
   __device__ __forceinline__ int getp(int p) const {
@@ -1094,23 +1098,8 @@ __global__ void __launch_bounds__(MAXT, 1)
     const int imm8 = (w >> 8) & 0xFF;
     const int imm16 = (w >> 8) & 0xFFFF;
     const int fam = (w >> 24) & 31;
-    const int rmode = w >> 29;
-    // ---- memory reads ----
-    int v1 = 0, v2 = 0;
-    if (rmode != RD_NONE) {
-      int ra;
-      switch (rmode) {
-        case RD_HL: ra = h.HL(); break;
-        case RD_BC: ra = h.BC(); break;
-        case RD_DE: ra = h.DE(); break;
-        case RD_A16: ra = imm16; break;
-        case RD_FF_N: ra = 0xFF00 | imm8; break;
-        case RD_FF_C: ra = 0xFF00 | h.C_(); break;
-        default: ra = h.sp; break;
-      }
-      v1 = rd(ra);
-      if (rmode == RD_SP) v2 = rd((ra + 1) & 0xFFFF);
-    }
+    // Memory operands are read inside the families that have them (reads
+    // have no side effects, so RET cc reads the stack only when taken).
     // ---- execute ----
     int npc = pc + 1;
     int cyc = 4;
@@ -1132,14 +1121,15 @@ __global__ void __launch_bounds__(MAXT, 1)
         else { wa0 = imm16; npc = pc + 3; cyc = 16; }
         break;
       case FM_LD_A:
-        h.setA(v1);
         if (opcode < 0x40) {
-          const int p = (opcode >> 4) & 3;
-          if (p >= 2) { const int hl = h.HL(); h.setHL(p == 2 ? hl + 1 : hl - 1); }
+          const int p = (opcode >> 4) & 3;  // 0 BC, 1 DE, 2 HL+, 3 HL-
+          const int ad = p == 0 ? h.BC() : p == 1 ? h.DE() : h.HL();
+          h.setA(rd(ad));
+          if (p >= 2) h.setHL(p == 2 ? ad + 1 : ad - 1);
           cyc = 8;
-        } else if (opcode == 0xF0) { npc = pc + 2; cyc = 12; }
-        else if (opcode == 0xF2) { cyc = 8; }
-        else { npc = pc + 3; cyc = 16; }
+        } else if (opcode == 0xF0) { h.setA(rd(0xFF00 | imm8)); npc = pc + 2; cyc = 12; }
+        else if (opcode == 0xF2) { h.setA(rd(0xFF00 | h.C_())); cyc = 8; }
+        else { h.setA(rd(imm16)); npc = pc + 3; cyc = 16; }
         break;
       case FM_INCDEC16: {
         const int p = (opcode >> 4) & 3;
@@ -1154,7 +1144,7 @@ __global__ void __launch_bounds__(MAXT, 1)
         break;
       }
       case FM_INCDEC_HL: {
-        const int old = v1, dec1 = z & 1;
+        const int old = rd(h.HL()), dec1 = z & 1;
         const int v = (dec1 ? old - 1 : old + 1) & 0xFF;
         h.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (h.f >> 4) & 1);
         nw = 1; wa0 = h.HL(); wv0 = v;
@@ -1206,19 +1196,19 @@ __global__ void __launch_bounds__(MAXT, 1)
         else h.f = FLAGS(zf, 0, 0, y == 6 ? 1 : !cf);
         break;
       }
-      case FM_LDR_HL: h.setr(y, v1); cyc = 8; break;
+      case FM_LDR_HL: h.setr(y, rd(h.HL())); cyc = 8; break;
       case FM_STHL_R: nw = 1; wa0 = h.HL(); wv0 = h.getr(z); cyc = 8; break;
       case FM_HALT: s.halted = 1; s.ev |= EV_HALT; h.next_ev = INT_MIN; break;
       case FM_ALU_R: h.alu(y, h.getr(z)); break;
       case FM_ALU_V: {
-        const bool hl = rmode == RD_HL;
-        h.alu(y, hl ? v1 : imm8);
+        const bool hl = opcode < 0xC0;  // ALU A,(HL); else ALU A,d8
+        h.alu(y, hl ? rd(h.HL()) : imm8);
         npc = pc + (hl ? 1 : 2);
         cyc = 8; break;
       }
       case FM_RET:
         if (opcode == 0xC9 || opcode == 0xD9 || h.cond(y)) {
-          npc = v1 | (v2 << 8);
+          npc = rd(h.sp) | (rd((h.sp + 1) & 0xFFFF) << 8);
           h.sp = (h.sp + 2) & 0xFFFF;
           if (opcode == 0xD9) { s.ime = 1; s.ime_delay = 0; s.ev |= EV_IRQ; h.next_ev = INT_MIN; }
           cyc = (opcode & 1) ? 16 : 20;
@@ -1228,6 +1218,7 @@ __global__ void __launch_bounds__(MAXT, 1)
         break;
       case FM_POP: {
         const int p = (opcode >> 4) & 3;
+        const int v1 = rd(h.sp), v2 = rd((h.sp + 1) & 0xFFFF);
         if (p == 3) { h.setA(v2); h.f = v1 & 0xF0; }
         else h.setp(p, v1 | (v2 << 8));
         h.sp = (h.sp + 2) & 0xFFFF;
@@ -1268,7 +1259,7 @@ __global__ void __launch_bounds__(MAXT, 1)
         // bitops.py: RLC RRC RL RR SLA SRA SWAP SRL, BIT, RES, SET
         const int cb = imm8, cz = cb & 7, cy = (cb >> 3) & 7, grp = cb >> 6;
         const bool hl = cz == 6;
-        const int v = hl ? v1 : h.getr(cz);
+        const int v = hl ? rd(h.HL()) : h.getr(cz);
         npc = pc + 2;
         if (grp == 1) {  // BIT: Z from the bit, H set, C kept
           h.f = ((((v >> cy) & 1) ^ 1) << 7) | 0x20 | (h.f & 0x10);
