@@ -279,6 +279,7 @@ struct Emu {
     win_lo = bootrom ? 0x100 : 0;
     int hi = 0;
     if (bank0_off == 0) hi = (bankN_off == 0 && pre_s_words >= 0x8000) ? 0x7FFE : 0x3FFE;
+    if (hi > pre_s_words) hi = pre_s_words;  // only the staged words are in shared memory
     win_len = hi > win_lo ? hi - win_lo : 0;
     // A000-BFFF as plain bytes when it maps a whole bank of cart RAM
     // (ram_index / cart_read with RAM enabled and no RTC register selected)
@@ -1446,7 +1447,9 @@ static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int
   per_block = per_block < 1 ? 1 : per_block > 32 ? 32 : per_block;
   const int threads = per_block * 32;
   const int blocks = (int)((warps + per_block - 1) / per_block);
-  const int rom_words = st.rom_bytes < ROM_SMEM_MAX ? st.rom_bytes : ROM_SMEM_MAX;
+  int stage_words = env_int("GBX_ROM_SMEM_WORDS", ROM_SMEM_MAX);  // experiments: staged ROM size
+  stage_words = stage_words < 0x400 ? 0x400 : stage_words > 0x8000 ? 0x8000 : stage_words & ~0xFF;
+  const int rom_words = st.rom_bytes < stage_words ? st.rom_bytes : stage_words;
   const size_t sm = (size_t)rom_words * 4 + 512;
   if (threads <= 256)
     return launch_t<MBC, 256>(st, pre, actions, frames, release, stage, stream, K, threads, blocks, rom_words, sm);
