@@ -13,9 +13,10 @@ import ctypes
 from ctypes import POINTER, c_char_p, c_int32, c_int64, c_size_t, c_uint32, c_void_p
 
 GBX_OK, GBX_ERR_INVALID, GBX_ERR_CUDA, GBX_ERR_OOM, GBX_ERR_STATE, GBX_ERR_RANGE = range(6)
+ABI_VERSION = 2  # include/gbx.h GBX_ABI_VERSION
 
 BUF = {"mem": 0, "pixels": 1, "pixels_packed": 2, "obs": 3, "reward": 4, "cart_ram": 5,
-       "serial": 6, "i32": 7, "i64": 8, "u8": 9, "cart_state": 10, "latch": 11}
+       "serial": 6, "i32": 7, "i64": 8, "u8": 9, "cart_state": 10, "latch": 11, "frame_bg": 12}
 I32_FIELDS = ("pc", "sp", "a", "b", "c", "d", "e", "h", "l", "f", "cycle_in_frame", "trap_flag",
               "trap_pc", "trap_opcode", "trap_kind", "serial_len", "ime", "ime_delay", "halted",
               "div_counter", "timer_prev_in", "tima_reload_pending", "tima_reload_delay",
@@ -78,13 +79,15 @@ def lib():
         "gbx_import_state": ([P, c_int32, c_int32, POINTER(HostState)], c_int32),
         "gbx_read_mem": ([P, c_int32, c_int32, c_int32, P], c_int32),
         "gbx_device_status": ([P, POINTER(c_uint32), c_int32], c_int32),
+        "gbx_render_bg_env0": ([P, P, P], c_int32),
+        "gbx_set_debug_traps": ([P, c_int32, c_int32, c_int64, c_int32], c_int32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
         fn.argtypes = args
         fn.restype = res
-    if L.gbx_abi_version() != 1:
-        raise RuntimeError(f"libgbx ABI {L.gbx_abi_version()} != 1")
+    if L.gbx_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"libgbx ABI {L.gbx_abi_version()} != {ABI_VERSION}")
     _lib = L
     return L
 

@@ -30,6 +30,7 @@ import numpy as np
 
 from . import _lib as L
 from . import cartridge as cart
+from .debug_traps import read_debug_env
 from .roms import boot_stub
 from .state import LATCHES, MEM_SIZE, OBS_DIM, SCALARS, SERIAL_MAX
 
@@ -83,8 +84,6 @@ class GbxVecCudaBackend:
             raise ValueError(f"unknown stage {stage!r}")
         if action_codec not in ACTION_CODECS:
             raise ValueError(f"Unknown action codec: {action_codec}")
-        if render_bg:
-            raise NotImplementedError("render_bg (env-0 scanline BG frame) is not built yet")
         self.num_envs = int(num_envs)
         if self.num_envs <= 0:
             raise ValueError(f"num_envs must be > 0, got {num_envs}")
@@ -94,10 +93,14 @@ class GbxVecCudaBackend:
         self._release_after_frames = int(release_after_frames)
         self._base_seed = base_seed
         self._stage = stage
+        self._render_bg = bool(render_bg)
         self._render_pixels = bool(render_pixels)
         self._render_pixels_packed = bool(render_pixels_packed)
         self._render_on_step = bool(render_on_step)
         self._force_lcdc_on_render = bool(force_lcdc_on_render)
+        # GBXCULE_TRAP_* / _MAX_INSTR / _WATCH_ADDR, read when the backend is
+        # built, as the reference does when it fetches its kernel (warp_vec.py:140)
+        self._debug = read_debug_env()
         self.action_codec = action_codec
         self.num_actions = len(ACTION_CODECS[action_codec])
         self.device = "cuda"
@@ -164,6 +167,9 @@ class GbxVecCudaBackend:
         bb = (ctypes.c_uint8 * 256).from_buffer_copy(boot)
         L.check(self._lib.gbx_create(ctypes.byref(cfg), rb, len(rom), bb, 256, ctypes.byref(h)), "gbx_create")
         self._h = h
+        d = self._debug
+        L.check(self._lib.gbx_set_debug_traps(h, d.trap_pc, d.trap_rst38, d.max_instr, d.watch_addr),
+                "gbx_set_debug_traps")
         self._spec = spec
         self._rom_bytes, self._bootrom_bytes = rom, boot
         info = L.Info()
@@ -205,6 +211,8 @@ class GbxVecCudaBackend:
         release = self._release_after_frames if release is None else release
         s = self._stream()
         L.check(self._lib.gbx_step(self._h, ctypes.c_void_p(actions_ptr), int(frames), int(release), s), "gbx_step")
+        if render and self._render_bg:  # env-0 frame from the scanline latches (warp_vec.py:651-671)
+            L.check(self._lib.gbx_render_bg_env0(self._h, None, s), "gbx_render_bg_env0")
         if render and self._render_on_step:
             self._launch_render_pixels()
 
@@ -481,6 +489,16 @@ class GbxVecCudaBackend:
         self._need()
         self._torch().cuda.synchronize(self._ordinal)
         return self._view("i32")[0].cpu().numpy().copy()
+
+    def read_frame_bg_shade_env0(self) -> bytes:
+        """Env 0's 160x144 frame, row-major, one shade per byte (warp_vec.py:1389-1404).
+
+        Rendered after each step when the backend was built with
+        ``render_bg=True``; zeros before the first such step.
+        """
+        self._need()
+        self._torch().cuda.synchronize(self._ordinal)
+        return self._view("frame_bg").cpu().numpy().tobytes()
 
     def read_serial(self, env_idx: int) -> bytes:
         if env_idx < 0 or env_idx >= self.num_envs:

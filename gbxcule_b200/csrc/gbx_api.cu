@@ -15,7 +15,8 @@
 
 namespace gbx {
 cudaError_t launch_step(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames, int release,
-                        int stage, cudaStream_t stream);
+                        int stage, cudaStream_t stream, const DebugCfg& dbg);
+cudaError_t launch_render_bg_env0(const DevState& st, uint8_t* out, cudaStream_t stream);
 void predecode_rom(const uint8_t* rom, int n, uint32_t* out);
 cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
                           cudaStream_t stream);
@@ -38,6 +39,8 @@ struct gbx_env {
   uint8_t* pix;
   uint8_t* pix_packed;
   uint32_t* pre;           // pre-decoded ROM, one word per byte (gbx_step.cu)
+  uint8_t* frame_bg;       // env-0 160x144 frame
+  DebugCfg dbg;            // debug traps (all off by default)
   bool initialized;
 };
 
@@ -125,7 +128,8 @@ int dalloc(T** p, size_t count) {
 void free_env(gbx_env* h) {
   DevState& st = h->st;
   void* ptrs[] = {(void*)st.rom, (void*)st.boot, st.mem, st.cart_ram, st.serial, st.cart_state, st.i32,
-                  st.i64, st.u8s, st.latch, st.obs, st.reward, st.status, h->pix, h->pix_packed, h->pre};
+                  st.i64, st.u8s, st.latch, st.obs, st.reward, st.status, h->pix, h->pix_packed, h->pre,
+                  h->frame_bg};
   for (void* p : ptrs)
     if (p) cudaFree(p);
 }
@@ -141,6 +145,7 @@ int zero_state(gbx_env* h, cudaStream_t s) {
   CK(cudaMemsetAsync(st.i64, 0, sizeof(int64_t) * I64_COUNT * S, s), "memset i64");
   CK(cudaMemsetAsync(st.u8s, 0, (size_t)U8_COUNT * S, s), "memset u8");
   CK(cudaMemsetAsync(st.latch, 0, 9 * SCREEN_H, s), "memset latch");
+  CK(cudaMemsetAsync(h->frame_bg, 0, 160 * SCREEN_H, s), "memset frame_bg");
   CK(cudaMemsetAsync(st.obs, 0, sizeof(float) * OBS_DIM * (size_t)st.n, s), "memset obs");
   CK(cudaMemsetAsync(st.reward, 0, sizeof(float) * (size_t)st.n, s), "memset reward");
   CK(cudaMemsetAsync(st.status, 0, sizeof(uint32_t), s), "memset status");
@@ -248,7 +253,7 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
   }
   st.rom = rom_d;
   st.boot = boot_d;
-  if ((rc = dalloc(&h->pre, (size_t)rom_bytes))) {
+  if ((rc = dalloc(&h->frame_bg, (size_t)160 * SCREEN_H)) || (rc = dalloc(&h->pre, (size_t)rom_bytes))) {
     free_env(h);
     delete h;
     return rc;
@@ -307,7 +312,7 @@ int gbx_reset(gbx_env* h, void* stream) {
   h->initialized = true;
   if (h->cfg.stage == STAGE_OBS || h->cfg.stage == STAGE_FULL) {
     const int32_t* zero_actions = h->st.i32 + (size_t)F_ACTIONS * h->st.S;
-    CK(launch_step(h->st, h->pre, zero_actions, 0, 0, h->cfg.stage, s), "step kernel (reset obs)");
+    CK(launch_step(h->st, h->pre, zero_actions, 0, 0, h->cfg.stage, s, h->dbg), "step kernel (reset obs)");
   }
   return GBX_OK;
 }
@@ -318,7 +323,7 @@ int gbx_step(gbx_env* h, const int32_t* actions, int32_t frames, int32_t release
   if (frames < 0) return fail(GBX_ERR_INVALID, "frames_to_run must be >= 0, got %d", frames);
   if (frames > 25000) return fail(GBX_ERR_INVALID, "frames_to_run %d exceeds 25000 per launch", frames);
   DeviceGuard g(h->cfg.device);
-  CK(launch_step(h->st, h->pre, actions, frames, release, h->cfg.stage, S_(stream)), "step kernel");
+  CK(launch_step(h->st, h->pre, actions, frames, release, h->cfg.stage, S_(stream), h->dbg), "step kernel");
   return GBX_OK;
 }
 
@@ -432,6 +437,7 @@ int gbx_buffer(const gbx_env* h, int32_t which, gbx_buffer_info* o) {
     case GBX_BUF_U8: set(st.u8s, 1, 8, 2, U8_COUNT, n, 0, S, 1, 0); break;
     case GBX_BUF_CART_STATE: set(st.cart_state, 0, 32, 2, CS_STRIDE, n, 0, S, 1, 0); break;
     case GBX_BUF_LATCH: set(st.latch, 1, 8, 2, 9, SCREEN_H, 0, SCREEN_H, 1, 0); break;
+    case GBX_BUF_FRAME_BG: set(h->frame_bg, 1, 8, 2, SCREEN_H, 160, 0, 160, 1, 0); break;
     default: return fail(GBX_ERR_INVALID, "unknown buffer id %d", which);
   }
   return GBX_OK;
@@ -527,6 +533,23 @@ int gbx_read_mem(gbx_env* h, int32_t env_idx, int32_t lo, int32_t hi, uint8_t* h
   CK(cudaDeviceSynchronize(), "sync before read");
   const uint8_t* src = h->st.mem + (size_t)env_idx * MEM_SIZE + lo;
   CK(cudaMemcpy(host_out, src, (size_t)(hi - lo), cudaMemcpyDeviceToHost), "read copy");
+  return GBX_OK;
+}
+
+int gbx_render_bg_env0(gbx_env* h, uint8_t* out, void* stream) {
+  RET(check_init(h));
+  DeviceGuard g(h->cfg.device);
+  CK(launch_render_bg_env0(h->st, out ? out : h->frame_bg, S_(stream)), "render_bg kernel");
+  return GBX_OK;
+}
+
+int gbx_set_debug_traps(gbx_env* h, int32_t trap_pc, int32_t trap_rst38, int64_t max_instr, int32_t watch_addr) {
+  RET(check_env(h));
+  if (max_instr < 0) return fail(GBX_ERR_INVALID, "max_instr must be >= 0, got %lld", (long long)max_instr);
+  h->dbg.trap_pc = trap_pc & 0xFFFF;
+  h->dbg.trap_rst38 = trap_rst38 ? 1 : 0;
+  h->dbg.max_instr = max_instr;
+  h->dbg.watch_addr = watch_addr & 0xFFFF;
   return GBX_OK;
 }
 

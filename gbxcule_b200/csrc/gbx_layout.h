@@ -88,6 +88,16 @@ struct DevState {
   uint32_t* status;
 };
 
+// Debug traps of the reference kernel (cpu_step_builder.py:1320-1393,
+// configured from GBXCULE_TRAP_PC / _TRAP_RST38 / _MAX_INSTR / _WATCH_ADDR by
+// cpu_step.py:85-105); 0 = off. Trap kinds: 5 pc, 3 RST 38, 4 jump into
+// FE00-FFFF, 6 instruction budget, 7 watched byte changed.
+struct DebugCfg {
+  int32_t trap_pc, trap_rst38, watch_addr;
+  int64_t max_instr;
+  __host__ __device__ bool active() const { return trap_pc || trap_rst38 || watch_addr || max_instr > 0; }
+};
+
 // Device-resident copy of one env (ResetCache, src/gbxcule/core/reset_cache.py:22-64).
 struct Snapshot {
   uint8_t* mem;         // [65536]

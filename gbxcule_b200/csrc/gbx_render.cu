@@ -137,6 +137,84 @@ __global__ void __launch_bounds__(RENDER_THREADS) render_kernel(DevState st, uin
   }
 }
 
+// --- env 0's 160x144 frame (kernels/ppu_step.py:11-176) ---------------------
+// One block per scanline y, one thread per pixel. The line's registers come
+// from the env-0 scanline latches (LCDC, SCX, SCY, BGP, WX, WY, window line,
+// OBP0, OBP1 captured when the line started); VRAM and OAM are env 0's
+// current memory. The window row is the latched window line counter (the
+// downsampled renderer uses y - WY instead). Sprites: the first 10 in OAM
+// order that pass the validity and line tests, smallest X then lowest OAM
+// index among opaque pixels, OBJ-to-BG priority against the raw BG colour.
+__global__ void __launch_bounds__(160) render_bg_env0_kernel(DevState st, uint8_t* __restrict__ out) {
+  __shared__ uint8_t oam[160];
+  __shared__ uint32_t spr[MAX_SPR];  // left+8 | lo<<8 | hi<<16 | attr<<24, OAM order
+  __shared__ int nspr_s;
+  const int y = blockIdx.x, x = threadIdx.x;
+  const uint8_t* m = st.mem;  // env 0
+  const uint8_t* L = st.latch;
+  const int lcdc = L[0 * SCREEN_H + y], scx = L[1 * SCREEN_H + y], scy = L[2 * SCREEN_H + y];
+  const int bgp = L[3 * SCREEN_H + y], wx = L[4 * SCREEN_H + y], wy = L[5 * SCREEN_H + y];
+  const int win_line = L[6 * SCREEN_H + y], obp0 = L[7 * SCREEN_H + y], obp1 = L[8 * SCREEN_H + y];
+  oam[x] = m[0xFE00 + x];
+  __syncthreads();
+  if (x == 0) {
+    int n = 0;
+    if (lcdc & 2) {
+      const int sh = (lcdc & 4) ? 16 : 8;
+      for (int k = 0; k < 40 && n < MAX_SPR; k++) {
+        const int sy = oam[4 * k], sx = oam[4 * k + 1];
+        if (sx == 0 || sy == 0 || sx >= 168 || sy >= 160) continue;
+        const int top = sy - 16;
+        if (y < top || y >= top + sh) continue;
+        int tile = oam[4 * k + 2];
+        const int attr = oam[4 * k + 3];
+        int row = y - top;
+        if ((attr >> 6) & 1) row = sh - 1 - row;
+        if (sh == 16) { tile &= 0xFE; if (row >= 8) { tile++; row -= 8; } }
+        const int ta = 0x8000 + tile * 16 + row * 2;
+        spr[n++] = (uint32_t)sx | ((uint32_t)m[ta] << 8) | ((uint32_t)m[ta + 1] << 16) | ((uint32_t)attr << 24);
+      }
+    }
+    nspr_s = n;
+  }
+  __syncthreads();
+  int shade = 0, bg_color = 0;
+  if (lcdc & 1) {
+    int px, py, map;
+    if ((lcdc & 0x20) && y >= wy && x >= wx - 7) {
+      px = x - (wx - 7); py = win_line; map = (lcdc & 0x40) ? 0x9C00 : 0x9800;
+    } else {
+      px = (x + scx) & 0xFF; py = (y + scy) & 0xFF; map = (lcdc & 0x08) ? 0x9C00 : 0x9800;
+    }
+    const int tid = m[map + ((py & 0xFF) >> 3) * 32 + ((px & 0xFF) >> 3)];
+    int ta = (lcdc & 0x10) ? 0x8000 + tid * 16 : 0x9000 + (tid >= 128 ? tid - 256 : tid) * 16;
+    ta += (py & 7) * 2;
+    const int bit = 7 - (px & 7);
+    bg_color = (((m[ta + 1] >> bit) & 1) << 1) | ((m[ta] >> bit) & 1);
+    shade = (bgp >> (bg_color * 2)) & 3;
+  }
+  int best_left = 1 << 30, best_color = 0, best_attr = 0;
+  for (int j = 0; j < nspr_s; j++) {
+    const uint32_t e = spr[j];
+    const int left = (int)(e & 0xFF) - 8;
+    if (x < left || x >= left + 8 || left >= best_left) continue;
+    const int attr = e >> 24, lo = (e >> 8) & 0xFF, hi = (e >> 16) & 0xFF;
+    const int pxo = x - left;
+    const int bit = ((attr >> 5) & 1) ? pxo : 7 - pxo;
+    const int color = (((hi >> bit) & 1) << 1) | ((lo >> bit) & 1);
+    if (color == 0) continue;
+    best_left = left; best_color = color; best_attr = attr;
+  }
+  if (best_color && !(((best_attr >> 7) & 1) && bg_color != 0))
+    shade = ((((best_attr >> 4) & 1) ? obp1 : obp0) >> (best_color * 2)) & 3;
+  out[y * 160 + x] = (uint8_t)shade;
+}
+
+cudaError_t launch_render_bg_env0(const DevState& st, uint8_t* out, cudaStream_t stream) {
+  render_bg_env0_kernel<<<SCREEN_H, 160, 0, stream>>>(st, out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
                           cudaStream_t stream) {
   // every env image starts 16-byte aligned when the buffer start is (1440 and 5760 are multiples of 16)

@@ -918,13 +918,15 @@ struct Emu {
     }
     return frames_done >= frames_to_run;
   }
-  // unimplemented opcode (misc.py:42-56)
-  __device__ __noinline__ void trap_op(int at, int op) {
+  // unimplemented opcode (misc.py:42-56, kind 1) or a debug trap; the first
+  // trap of an env keeps its pc, opcode and kind
+  __device__ __noinline__ void trap_op(int at, int op, int kind) {
+    if (trap) return;
     trap = 1;
     ev |= EV_TRAP;
     i32[(size_t)F_TRAP_PC * S] = at & 0xFFFF;
     i32[(size_t)F_TRAP_OPCODE * S] = op & 0xFF;
-    i32[(size_t)F_TRAP_KIND * S] = 1;
+    i32[(size_t)F_TRAP_KIND * S] = kind;
   }
 };
 
@@ -937,10 +939,12 @@ __device__ __forceinline__ int sign8(int v) { return v >= 128 ? v - 256 : v; }
 // spreads few envs over many warps (no divergence, more latency hiding);
 // K = 32 packs a full warp (shared issue slots when envs run in lockstep).
 // MAXT = largest block size the launch may use (caps registers at 64K/MAXT).
-template <int MBC, int MAXT>
+// DBG = the debug-trap instantiation (launched only when a trap is set).
+template <int MBC, int MAXT, bool DBG>
 __global__ void __launch_bounds__(MAXT, 1)
     gb_step_kernel(DevState st, const uint32_t* __restrict__ pre_g, const int32_t* __restrict__ actions,
-                   int frames_to_run, int release_after_frames, int stage, int K, int pre_s_words) {
+                   int frames_to_run, int release_after_frames, int stage, int K, int pre_s_words,
+                   DebugCfg dbg) {
   extern __shared__ __align__(16) uint8_t smem[];
   uint32_t* pre_s = reinterpret_cast<uint32_t*>(smem);
   uint8_t* boot_s = smem + (size_t)pre_s_words * 4;
@@ -1047,6 +1051,9 @@ __global__ void __launch_bounds__(MAXT, 1)
     run = s.frames_done < frames_to_run;
   }
 
+  // watched byte at launch start (cpu_step_builder.py:948-951)
+  const int watch_val = (DBG && dbg.watch_addr) ? s.raw_read(dbg.watch_addr & 0xFFFF) : 0;
+
   // ---- interpreter loop: registers in h, cold state in s ----
   Hot h;
   h.bcde = s.bcde; h.hlxa = s.hlxa; h.f = s.f; h.pc = s.pc; h.sp = s.sp;
@@ -1099,6 +1106,10 @@ __global__ void __launch_bounds__(MAXT, 1)
     const int imm8 = (w >> 8) & 0xFF;
     const int imm16 = (w >> 8) & 0xFFFF;
     const int fam = (w >> 24) & 31;
+    if (DBG) {  // checks before execution (:1320-1338)
+      if (dbg.trap_pc && pc == dbg.trap_pc) { s.trap_op(pc, opcode, 5); break; }
+      if (dbg.trap_rst38 && opcode == 0xFF && pc != 0x0038) { s.trap_op(pc, opcode, 3); break; }
+    }
     // Memory operands are read inside the families that have them (reads
     // have no side effects, so RET cc reads the stack only when taken).
     // ---- execute ----
@@ -1305,7 +1316,7 @@ __global__ void __launch_bounds__(MAXT, 1)
         else s.ime = 0;
         break;
       default:  // FM_TRAP (misc.py:42-56)
-        s.trap_op(pc, opcode);
+        s.trap_op(pc, opcode, 1);
         h.next_ev = INT_MIN;
         npc = pc;
         cyc = 0;
@@ -1318,8 +1329,18 @@ __global__ void __launch_bounds__(MAXT, 1)
       if (nw == 2) wr(wa1, wv1);
     }
     // ---- tail ----
-    h.clk += cyc;
     ninstr++;
+    if (DBG) {  // checks after execution (:1362-1393); a trapping instruction's cycles never run
+      if (dbg.trap_rst38 && h.pc >= 0xFE00) { s.trap_op(pc, opcode, 4); ninstr--; break; }
+      if (s.trap) { ninstr--; break; }
+      if (dbg.max_instr > 0 && ninstr >= dbg.max_instr) { s.trap_op(h.pc, opcode, 6); break; }
+      if (dbg.watch_addr) {
+        const int a = dbg.watch_addr & 0xFFFF;
+        s.clk = h.clk;
+        if (s.raw_read(a) != watch_val) { s.trap_op(pc, opcode, 7); break; }
+      }
+    }
+    h.clk += cyc;
     if (h.clk >= h.next_ev) {
       if (s.trap) { ninstr--; break; }
       save();
@@ -1425,21 +1446,21 @@ int step_envs_per_warp(int n) {
   return n <= 3 * wave ? 1 : 32;
 }
 
-template <int MBC, int MAXT>
+template <int MBC, int MAXT, bool DBG>
 static cudaError_t launch_t(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames,
                             int release, int stage, cudaStream_t stream, int K, int threads, int blocks,
-                            int pre_s_words, size_t sm) {
-  cudaError_t e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sm);
+                            int pre_s_words, size_t sm, const DebugCfg& dbg) {
+  cudaError_t e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT, DBG>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
-  gb_step_kernel<MBC, MAXT><<<blocks, threads, sm, stream>>>(st, pre, actions, frames, release, stage, K,
-                                                            pre_s_words);
+  gb_step_kernel<MBC, MAXT, DBG><<<blocks, threads, sm, stream>>>(st, pre, actions, frames, release, stage, K,
+                                                                 pre_s_words, dbg);
   return cudaGetLastError();
 }
 
 template <int MBC>
 static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames,
-                              int release, int stage, cudaStream_t stream) {
+                              int release, int stage, cudaStream_t stream, const DebugCfg& dbg) {
   const int K = step_envs_per_warp(st.n);
   const long long warps = (st.n + K - 1) / K;
   // one block per SM (the pre-decoded banks fill shared memory): spread warps
@@ -1451,19 +1472,25 @@ static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int
   stage_words = stage_words < 0x400 ? 0x400 : stage_words > 0x8000 ? 0x8000 : stage_words & ~0xFF;
   const int rom_words = st.rom_bytes < stage_words ? st.rom_bytes : stage_words;
   const size_t sm = (size_t)rom_words * 4 + 512;
+  if (dbg.active())  // debug traps: one instantiation (its 64-register bound fits every block size)
+    return launch_t<MBC, 1024, true>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
+                                     rom_words, sm, dbg);
   if (threads <= 256)
-    return launch_t<MBC, 256>(st, pre, actions, frames, release, stage, stream, K, threads, blocks, rom_words, sm);
+    return launch_t<MBC, 256, false>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
+                                     rom_words, sm, dbg);
   if (threads <= 512)
-    return launch_t<MBC, 512>(st, pre, actions, frames, release, stage, stream, K, threads, blocks, rom_words, sm);
-  return launch_t<MBC, 1024>(st, pre, actions, frames, release, stage, stream, K, threads, blocks, rom_words, sm);
+    return launch_t<MBC, 512, false>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
+                                     rom_words, sm, dbg);
+  return launch_t<MBC, 1024, false>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
+                                    rom_words, sm, dbg);
 }
 
 cudaError_t launch_step(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames, int release,
-                        int stage, cudaStream_t stream) {
+                        int stage, cudaStream_t stream, const DebugCfg& dbg) {
   switch (st.mbc_kind) {
-    case MBC_MBC1: return launch_mbc<MBC_MBC1>(st, pre, actions, frames, release, stage, stream);
-    case MBC_MBC3: return launch_mbc<MBC_MBC3>(st, pre, actions, frames, release, stage, stream);
-    default: return launch_mbc<MBC_ROM_ONLY>(st, pre, actions, frames, release, stage, stream);
+    case MBC_MBC1: return launch_mbc<MBC_MBC1>(st, pre, actions, frames, release, stage, stream, dbg);
+    case MBC_MBC3: return launch_mbc<MBC_MBC3>(st, pre, actions, frames, release, stage, stream, dbg);
+    default: return launch_mbc<MBC_ROM_ONLY>(st, pre, actions, frames, release, stage, stream, dbg);
   }
 }
 

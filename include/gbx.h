@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define GBX_ABI_VERSION 1
+#define GBX_ABI_VERSION 2
 
 typedef enum {
   GBX_OK = 0,
@@ -57,7 +57,8 @@ typedef enum {
   GBX_BUF_U8 = 9,             /* u8  [3, n]       strides [S, 1]    */
   GBX_BUF_CART_STATE = 10,    /* i32 [20, n]      strides [S, 1]    */
   GBX_BUF_LATCH = 11,         /* u8  [9, 144]     env-0 scanline latches */
-  GBX_BUF_COUNT = 12
+  GBX_BUF_FRAME_BG = 12,      /* u8  [144, 160]   env-0 frame (gbx_render_bg_env0) */
+  GBX_BUF_COUNT = 13
 } gbx_buffer_id;
 
 /* Rows of GBX_BUF_I32 (reference field names, warp_vec.py:342-419). */
@@ -178,6 +179,23 @@ int gbx_read_mem(gbx_env* env, int32_t env_idx, int32_t lo, int32_t hi, uint8_t*
 /* Device status word (bit 1: an env's cart_state mbc_kind differs from the
  * cartridge's); synchronous. Optionally clears it. */
 int gbx_device_status(gbx_env* env, uint32_t* out, int32_t clear);
+
+/* Env 0's 160x144 shade frame from the env-0 scanline latches and env 0's
+ * VRAM/OAM (kernels/ppu_step.py:11-176; launched after a step when the
+ * reference backend has render_bg=True, warp_vec.py:651-671). out: device
+ * u8[144*160], or NULL for the handle's own frame buffer (GBX_BUF_FRAME_BG,
+ * zeroed by gbx_reset). Enqueued on stream. */
+int gbx_render_bg_env0(gbx_env* env, uint8_t* out, void* stream);
+
+/* Debug traps of the reference kernel (cpu_step_builder.py:1320-1393), the
+ * values the reference reads from GBXCULE_TRAP_PC, GBXCULE_TRAP_RST38,
+ * GBXCULE_MAX_INSTR and GBXCULE_WATCH_ADDR (cpu_step.py:85-105); 0 turns a
+ * check off. Applies to every later gbx_step of the handle; a trapped env
+ * stops with trap_flag set and trap_kind 5 (pc), 3 (RST 38 outside 0x0038),
+ * 4 (jump into FE00-FFFF), 6 (max_instr instructions in one launch) or 7
+ * (watched byte changed). */
+int gbx_set_debug_traps(gbx_env* env, int32_t trap_pc, int32_t trap_rst38, int64_t max_instr,
+                        int32_t watch_addr);
 
 #ifdef __cplusplus
 }

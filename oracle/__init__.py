@@ -73,7 +73,16 @@ def _load():
         _lib.gbxo_step.argtypes = [ctypes.POINTER(_Ctx), ctypes.c_int32, ctypes.c_int32,
                                    ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
         _lib.gbxo_render.argtypes = [_P, ctypes.c_int32, _P, ctypes.c_int32, ctypes.c_int32]
+        _lib.gbxo_step_debug.argtypes = [ctypes.POINTER(_Ctx), ctypes.c_int32, ctypes.c_int32,
+                                         ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                         ctypes.POINTER(_Debug)]
+        _lib.gbxo_render_bg_env0.argtypes = [_P, _P * 9, _P]
     return _lib
+
+
+class _Debug(ctypes.Structure):
+    _fields_ = [("trap_pc", ctypes.c_int32), ("trap_rst38", ctypes.c_int32),
+                ("watch_addr", ctypes.c_int32), ("pad", ctypes.c_int32), ("max_instr", ctypes.c_int64)]
 
 
 def _ptr(a: np.ndarray):
@@ -92,6 +101,10 @@ class OracleEnvs:
         self.num_envs = int(num_envs)
         self.stage = stage
         self.threads = threads or os.cpu_count() or 1
+        from gbxcule_b200.debug_traps import read_debug_env
+
+        # the reference reads its debug-trap variables when the backend is built
+        self.debug = read_debug_env()
         self._lib = _load()
         self.reset()
 
@@ -142,8 +155,11 @@ class OracleEnvs:
 
     def _run(self, frames: int, release: int, lo: int = 0, hi: int | None = None) -> None:
         c = self._ctx()
-        self._lib.gbxo_step(ctypes.byref(c), lo, self.num_envs if hi is None else hi,
-                            frames, release, self.threads)
+        t = self.debug
+        d = _Debug(trap_pc=t.trap_pc, trap_rst38=t.trap_rst38, watch_addr=t.watch_addr, pad=0,
+                   max_instr=t.max_instr)
+        self._lib.gbxo_step_debug(ctypes.byref(c), lo, self.num_envs if hi is None else hi,
+                                  frames, release, self.threads, ctypes.byref(d))
 
     def step(self, actions: np.ndarray, frames: int = 24, release: int = 8) -> None:
         """One env-step for every env (``step_torch`` semantics: no range check)."""
@@ -155,6 +171,13 @@ class OracleEnvs:
         out = np.zeros(self.num_envs * 1440, dtype=np.uint8)
         self._lib.gbxo_render(_ptr(self.s["mem"]), self.num_envs, _ptr(out), 1, self.threads)
         return out.reshape(self.num_envs, 72, 20)
+
+    def render_bg_env0(self) -> np.ndarray:
+        """Env 0's 160x144 BG frame from the scanline latches (ppu_step.py:11-176)."""
+        out = np.zeros(144 * 160, dtype=np.uint8)
+        lat = (_P * 9)(*[_ptr(self.s[f"latch_{k}"]) for k in LATCHES])
+        self._lib.gbxo_render_bg_env0(_ptr(self.s["mem"]), lat, _ptr(out))
+        return out
 
     def render_shades(self) -> np.ndarray:
         out = np.zeros(self.num_envs * 5760, dtype=np.uint8)

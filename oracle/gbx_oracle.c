@@ -703,8 +703,21 @@ static void post_step(const gbxo_ctx *x, int i, const cpu_t *s) {
     }
 }
 
+/* Debug traps of the reference kernel (cpu_step.py:85-105 reads them from
+ * GBXCULE_TRAP_PC, GBXCULE_TRAP_RST38, GBXCULE_MAX_INSTR, GBXCULE_WATCH_ADDR;
+ * 0 = off). */
+typedef struct {
+    int32_t trap_pc, trap_rst38, watch_addr, pad;
+    int64_t max_instr;
+} gbxo_debug;
+
+static void set_trap(cpu_t *s, int pc, int op, int kind) {
+    if (s->trap == 0) { s->trap = 1; s->trap_pc = pc & 0xFFFF; s->trap_op = op & 0xFF; s->trap_kind = kind; }
+}
+
 /* The per-env body of cpu_step (:876-1781). */
-static void step_env(const gbxo_ctx *x, int i, int frames_to_run, int release_after_frames) {
+static void step_env(const gbxo_ctx *x, int i, int frames_to_run, int release_after_frames,
+                     const gbxo_debug *dbg) {
     envref rr = { x, i, (int64_t)i * MEM_SIZE, 0, release_after_frames };
     envref *r = &rr;
     uint8_t *m = x->mem + rr.base;
@@ -716,6 +729,8 @@ static void step_env(const gbxo_ctx *x, int i, int frames_to_run, int release_af
     int64_t instr = x->instr_count[i], cyc = x->cycle_count[i];
     int cycle_frame = x->cycle_in_frame[i];
     int scan = x->ppu_scanline_cycle[i], ly = x->ppu_ly[i], wl = x->ppu_window_line[i];
+    const int64_t instr_start = instr;                                   /* :946-951 */
+    const int watch_val = dbg->watch_addr ? m[dbg->watch_addr & 0xFFFF] : 0;
 
     while (rr.frames_done < frames_to_run) {
         if (s.trap) break;
@@ -755,6 +770,9 @@ static void step_env(const gbxo_ctx *x, int i, int frames_to_run, int release_af
         }
         int pc_before = s.pc;
         int opcode = read8(r, s.pc);
+        /* :1320-1338 checks before execution */
+        if (dbg->trap_pc && s.pc == dbg->trap_pc) { set_trap(&s, s.pc, opcode, 5); break; }
+        if (dbg->trap_rst38 && opcode == 0xFF && s.pc != 0x0038) { set_trap(&s, s.pc, opcode, 3); break; }
         int cycles;
         if (opcode == 0xCB) {
             int cb = read8(r, (s.pc + 1) & 0xFFFF);
@@ -763,9 +781,13 @@ static void step_env(const gbxo_ctx *x, int i, int frames_to_run, int release_af
         } else {
             cycles = exec_op(r, &s, opcode);
         }
+        /* :1362-1393 checks after execution */
+        if (dbg->trap_rst38 && s.pc >= 0xFE00) { set_trap(&s, pc_before, opcode, 4); break; }
         if (s.trap) break;
         s.f &= 0xF0;
         instr++;
+        if (dbg->max_instr > 0 && instr - instr_start >= dbg->max_instr) { set_trap(&s, s.pc, opcode, 6); break; }
+        if (dbg->watch_addr && m[dbg->watch_addr & 0xFFFF] != watch_val) { set_trap(&s, pc_before, opcode, 7); break; }
         timer_tick(r, cycles);
         if (x->ime_delay[i]) { x->ime[i] = 1; x->ime_delay[i] = 0; }
         int lcdc = ppu_advance(r, cycles, &scan, &ly, &wl);
@@ -823,13 +845,74 @@ static void step_env(const gbxo_ctx *x, int i, int frames_to_run, int release_af
 /* Exported entry points (ctypes)                                            */
 /* ------------------------------------------------------------------------ */
 
-void gbxo_step(const gbxo_ctx *x, int32_t env_lo, int32_t env_hi, int32_t frames_to_run,
-               int32_t release_after_frames, int32_t nthreads) {
+void gbxo_step_debug(const gbxo_ctx *x, int32_t env_lo, int32_t env_hi, int32_t frames_to_run,
+                     int32_t release_after_frames, int32_t nthreads, const gbxo_debug *dbg) {
 #ifdef _OPENMP
 #pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads > 0 ? nthreads : 1)
 #endif
-    for (int i = env_lo; i < env_hi; i++) step_env(x, i, frames_to_run, release_after_frames);
+    for (int i = env_lo; i < env_hi; i++) step_env(x, i, frames_to_run, release_after_frames, dbg);
     (void)nthreads;
+}
+
+void gbxo_step(const gbxo_ctx *x, int32_t env_lo, int32_t env_hi, int32_t frames_to_run,
+               int32_t release_after_frames, int32_t nthreads) {
+    const gbxo_debug off = {0, 0, 0, 0, 0};
+    gbxo_step_debug(x, env_lo, env_hi, frames_to_run, release_after_frames, nthreads, &off);
+}
+
+/* kernels/ppu_step.py:11-176: env 0's 160x144 frame from the per-line
+ * register latches (window row = the latched window line) and env 0's
+ * current VRAM/OAM. latch: lcdc, scx, scy, bgp, wx, wy, win_line, obp0, obp1. */
+void gbxo_render_bg_env0(const uint8_t *m, const uint8_t *const *latch, uint8_t *out) {
+    for (int y = 0; y < SCREEN_H; y++) {
+        const int lcdc = latch[0][y], scx = latch[1][y], scy = latch[2][y], bgp = latch[3][y];
+        const int wx = latch[4][y], wy = latch[5][y], win_line = latch[6][y];
+        const int obp0 = latch[7][y], obp1 = latch[8][y];
+        for (int x = 0; x < 160; x++) {
+            int shade = 0, bg_color = 0;
+            if (lcdc & 0x01) {
+                const int use_win = (lcdc & 0x20) && y >= wy && x >= wx - 7;
+                int px, py, map;
+                if (use_win) { px = x - (wx - 7); py = win_line; map = (lcdc & 0x40) ? 0x9C00 : 0x9800; }
+                else { px = (x + scx) & 0xFF; py = (y + scy) & 0xFF; map = (lcdc & 0x08) ? 0x9C00 : 0x9800; }
+                int tile_id = m[map + ((py & 0xFF) >> 3) * 32 + ((px & 0xFF) >> 3)];
+                int ta = (lcdc & 0x10) ? 0x8000 + tile_id * 16 : 0x9000 + (tile_id >= 128 ? tile_id - 256 : tile_id) * 16;
+                int row = py & 7;
+                int lo = m[ta + row * 2], hi = m[ta + row * 2 + 1];
+                int bit = 7 - (px & 7);
+                bg_color = (((hi >> bit) & 1) << 1) | ((lo >> bit) & 1);
+                shade = (bgp >> (bg_color * 2)) & 3;
+            }
+            if (lcdc & 0x02) {
+                const int sh = (lcdc & 0x04) ? 16 : 8;
+                int on_line = 0, found = 0, best_x = 0, best_color = 0, best_attr = 0;
+                for (int k = 0; k < 40; k++) {
+                    const int sy = m[0xFE00 + 4 * k], sx = m[0xFE00 + 4 * k + 1];
+                    int tile = m[0xFE00 + 4 * k + 2];
+                    const int attr = m[0xFE00 + 4 * k + 3];
+                    if (sx == 0 || sy == 0 || sx >= 168 || sy >= 160) continue;
+                    const int top = sy - 16, left = sx - 8;
+                    if (y < top || y >= top + sh) continue;
+                    if (on_line >= 10) continue;
+                    on_line++;
+                    if (x < left || x >= left + 8) continue;
+                    int row = y - top;
+                    if ((attr >> 6) & 1) row = sh - 1 - row;
+                    if (sh == 16) { tile &= 0xFE; if (row >= 8) { tile++; row -= 8; } }
+                    const int ta = 0x8000 + tile * 16;
+                    const int lo = m[ta + row * 2], hi = m[ta + row * 2 + 1];
+                    const int pxo = x - left;
+                    const int bit = ((attr >> 5) & 1) ? pxo : 7 - pxo;
+                    const int color = (((hi >> bit) & 1) << 1) | ((lo >> bit) & 1);
+                    if (color == 0) continue;
+                    if (!found || left < best_x) { found = 1; best_x = left; best_color = color; best_attr = attr; }
+                }
+                if (found && !(((best_attr >> 7) & 1) && bg_color != 0))
+                    shade = ((((best_attr >> 4) & 1) ? obp1 : obp0) >> (best_color * 2)) & 3;
+            }
+            out[y * 160 + x] = (uint8_t)shade;
+        }
+    }
 }
 
 /* ppu_render_downsampled.py:27-179 */

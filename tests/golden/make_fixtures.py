@@ -56,6 +56,10 @@ MICRO = [  # (name, frames_per_step, release_after_frames) from suite.yaml
 ]
 
 
+# unit 200 of config 1's loop: an instruction start every env reaches in the first step
+TRAP_PC_CONFIG1 = "0x0326"
+
+
 def _sha(b: bytes) -> str:
     return hashlib.sha256(b).hexdigest()
 
@@ -89,10 +93,30 @@ def run_case(args) -> dict:
     rom_path = tmp / "rom.gb"
     rom_path.write_bytes(rom_bytes)
     case["rom"]["sha256"] = _sha(rom_bytes)
-    ref = rh.load_reference(ref_root, boot)
+    # debug-trap cases set the reference's GBXCULE_* variables for this case
+    # only (pool workers are reused across cases); the reference reads them
+    # when the backend fetches its kernel
+    saved_env = {k: os.environ.get(k) for k in case.get("env", {})}
+    try:
+        return _run_case(ref_root, case, rom_bytes, rom_path, boot)
+    finally:
+        for k, v in saved_env.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+
+
+def _run_case(ref_root, case, rom_bytes, rom_path, boot) -> dict:
+    import ref_harness as rh
+
+    ref = rh.load_reference(ref_root, boot)  # clears any GBXCULE_* variables
+    os.environ.update(case.get("env", {}))
     n = case["num_envs"]
+    render_bg = case.get("render_bg", False)
     be = ref.backend(str(rom_path), num_envs=n, frames_per_step=case["frames"],
-                     release_after_frames=case["release"], stage=case["stage"])
+                     release_after_frames=case["release"], stage=case["stage"],
+                     render_bg=render_bg)
     t0 = time.time()
     be.reset()
     case["reset_digest"] = st.digest(_ref_state(be))
@@ -102,8 +126,10 @@ def run_case(args) -> dict:
 
     def do_step():
         act = _actions(case["actions"], rng, n)
-        ref.launch_step(be, act)
+        ref.launch_step(be, act, render=render_bg)
         rec = {"actions": act.tolist(), "digest": st.digest(_ref_state(be))}
+        if render_bg:
+            rec["frame_bg"] = _sha(ref.frame_bg(be).tobytes())
         if render:
             rec["render_packed"] = _sha(ref.render_packed(be).tobytes())
             rec["render_shades"] = _sha(ref.render_shades(be).tobytes())
@@ -163,6 +189,23 @@ def cases(micro: dict) -> list[dict]:
         dict(name="config5", rom={"kind": "config", "id": 5}, num_envs=4, frames=24, release=8,
              stage="obs_only", actions="uniform9", action_seed=5, steps=3, render=True),
     ]
+    # env-0 160x144 BG frame from the scanline latches (render_bg=True)
+    cs.append(dict(name="config2_bg", rom={"kind": "config", "id": 2}, num_envs=2, frames=24, release=8,
+                   stage="obs_only", actions="uniform9", action_seed=21, steps=3, render_bg=True))
+    cs.append(dict(name="micro_PPU_SPRITES_bg", rom={"kind": "micro", "id": "PPU_SPRITES"}, num_envs=2,
+                   frames=1, release=1, stage="obs_only", actions="uniform8", action_seed=22, steps=3,
+                   render_bg=True, _rom_hex=micro["PPU_SPRITES"].hex()))
+    cs.append(dict(name="micro_PPU_WINDOW_bg", rom={"kind": "micro", "id": "PPU_WINDOW"}, num_envs=2,
+                   frames=1, release=1, stage="obs_only", actions="uniform8", action_seed=23, steps=3,
+                   render_bg=True, _rom_hex=micro["PPU_WINDOW"].hex()))
+    # debug traps (GBXCULE_TRAP_PC / _TRAP_RST38 / _MAX_INSTR / _WATCH_ADDR)
+    for name, cfg, env in [("trap_pc", 1, {"GBXCULE_TRAP_PC": TRAP_PC_CONFIG1}),
+                           ("trap_rst38", 1, {"GBXCULE_TRAP_RST38": "1"}),
+                           ("trap_max_instr", 2, {"GBXCULE_MAX_INSTR": "30000"}),
+                           ("trap_watch", 1, {"GBXCULE_WATCH_ADDR": "0xDFEE"}),     # stack byte
+                           ("trap_watch_div", 2, {"GBXCULE_WATCH_ADDR": "0xFF04"})]:  # DIV register
+        cs.append(dict(name=name, rom={"kind": "config", "id": cfg}, num_envs=4, frames=24, release=8,
+                       stage="obs_only", actions="uniform9", action_seed=30 + cfg, steps=3, env=env))
     for name, frames, release in MICRO:
         steps = 3 if frames > 1 else 8
         cs.append(dict(name=f"micro_{name}", rom={"kind": "micro", "id": name}, num_envs=3,

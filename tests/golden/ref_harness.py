@@ -291,17 +291,23 @@ class Reference:
 
     def backend(self, rom_path: str, *, num_envs: int, frames_per_step: int,
                 release_after_frames: int, stage: str = "obs_only",
-                render_pixels: bool = False, render_pixels_packed: bool = False):
+                render_pixels: bool = False, render_pixels_packed: bool = False,
+                render_bg: bool = False):
         cls = self.m["warp_vec"].WarpVecCpuBackend
         return cls(rom_path, num_envs=num_envs, frames_per_step=frames_per_step,
                    release_after_frames=release_after_frames, stage=stage,
                    render_pixels=render_pixels, render_pixels_packed=render_pixels_packed,
-                   render_on_step=False)
+                   render_bg=render_bg, render_on_step=False)
 
-    def launch_step(self, be, actions: np.ndarray) -> None:
-        """``step_torch`` semantics: no host range check, one kernel launch."""
+    def launch_step(self, be, actions: np.ndarray, render: bool = False) -> None:
+        """``step_torch`` semantics: no host range check, one kernel launch
+        (plus the env-0 BG frame render when ``render`` and ``render_bg``)."""
         be._actions.assign(np.asarray(actions, dtype=np.int32))
-        be._launch_step(be._actions, render=False)
+        be._launch_step(be._actions, render=render)
+
+    def frame_bg(self, be) -> np.ndarray:
+        """The env-0 160x144 BG shade frame (``read_frame_bg_shade_env0``)."""
+        return np.frombuffer(be.read_frame_bg_shade_env0(), dtype=np.uint8).copy()
 
     def render_packed(self, be) -> np.ndarray:
         k = self.m["ppu"].ppu_render_shades_downsampled_packed_all_envs

@@ -24,10 +24,10 @@ def _declared():
 def test_library_exports_every_declared_symbol():
     lib = L.lib()
     names = _declared()
-    assert len(names) >= 18
+    assert len(names) >= 20
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.gbx_abi_version() == 1
+    assert lib.gbx_abi_version() == L.ABI_VERSION == 2
 
 
 def test_create_validates_before_touching_a_device():

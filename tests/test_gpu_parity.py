@@ -49,13 +49,15 @@ def _step(be, actions):
 
 
 @pytest.mark.parametrize("case", _cases(), ids=lambda c: c["name"])
-def test_golden_case_on_gpu(case, micro_roms):
+def test_golden_case_on_gpu(case, micro_roms, monkeypatch):
     from gbxcule_b200 import ResetCache
 
     rom = case_rom(case, micro_roms)
     n = case["num_envs"]
+    for k, v in case.get("env", {}).items():  # debug traps, read when the backend is built
+        monkeypatch.setenv(k, v)
     be = _backend(rom, n, case["frames"], case["release"], case["stage"], render_pixels=True,
-                  render_pixels_packed=True, render_on_step=False)
+                  render_pixels_packed=True, render_on_step=False, render_bg=case.get("render_bg", False))
     try:
         assert st.digest(be.export_state()) == case["reset_digest"]
         trace, warm = case["trace"], case.get("warmup", 0)
@@ -71,6 +73,8 @@ def test_golden_case_on_gpu(case, micro_roms):
         for k, rec in enumerate(trace[warm:]):
             _step(be, rec["actions"])
             assert st.digest(be.export_state()) == rec["digest"], f"step {k}"
+            if "frame_bg" in rec:
+                assert _sha(be.read_frame_bg_shade_env0()) == rec["frame_bg"], f"env-0 frame step {k}"
             if "render_packed" in rec:
                 be.render_pixels_snapshot_torch()
                 torch.cuda.synchronize()
@@ -263,5 +267,34 @@ def test_render_into_offset_buffer_matches_oracle():
             got = out[off:off + n * 1440].cpu().numpy().reshape(n, 72, 20)
             assert np.array_equal(got, o.render_packed())
             assert int(out[:off].sum()) == 0 and int(out[off + n * 1440:].sum()) == 0
+    finally:
+        be.close()
+
+
+def test_force_lcdc_on_render_matches_oracle():
+    """force_lcdc_on_render sets LCDC bit 7 in every env's memory before the
+    snapshot render (warp_vec.py:734-757); with the LCD switched off after the
+    ROM filled VRAM, the render shows the tiles and later steps run with the
+    LCD on, as in the reference."""
+    rom = roms.config2_rom()
+    n = 16
+    be = _backend(rom, n, 24, 8, render_pixels_packed=True, render_on_step=True, force_lcdc_on_render=True)
+    o = OracleEnvs(rom, roms.boot_stub(), n)
+    rng = np.random.default_rng(77)
+    try:
+        for _ in range(6):  # the ROM's VRAM set-up
+            a = roms.uniform_actions(rng, n)
+            _step(be, a)
+            o.step(a, 24, 8)
+        be.memory_torch()[:, 0xFF40] &= 0x7F
+        o.s["mem"].reshape(n, -1)[:, 0xFF40] &= 0x7F
+        for k in range(2):
+            a = roms.uniform_actions(rng, n)
+            _step(be, a)
+            o.step(a, 24, 8)
+            o.s["mem"].reshape(n, -1)[:, 0xFF40] |= 0x80  # the override before the render
+            torch.cuda.synchronize()
+            assert not st.diff(be.export_state(), o.state(), n), f"step {k}"
+            assert np.array_equal(be.pixels_packed_torch().cpu().numpy(), o.render_packed()), f"render {k}"
     finally:
         be.close()

@@ -31,9 +31,11 @@ def _cases():
 
 
 @pytest.mark.parametrize("case", _cases(), ids=lambda c: c["name"])
-def test_oracle_matches_reference(case, micro_roms):
+def test_oracle_matches_reference(case, micro_roms, monkeypatch):
     rom = case_rom(case, micro_roms)
     assert _sha(rom) == case["rom"]["sha256"], "ROM generator output changed"
+    for k, v in case.get("env", {}).items():  # debug traps, read at construction
+        monkeypatch.setenv(k, v)
     o = OracleEnvs(rom, roms.boot_stub(), case["num_envs"], stage=case["stage"])
     assert st.digest(o.state()) == case["reset_digest"]
     trace = case["trace"]
@@ -50,6 +52,8 @@ def test_oracle_matches_reference(case, micro_roms):
     for k, rec in enumerate(trace[warm:]):
         o.step(np.array(rec["actions"], dtype=np.int32), case["frames"], case["release"])
         assert st.digest(o.state()) == rec["digest"], f"step {k}"
+        if "frame_bg" in rec:
+            assert _sha(o.render_bg_env0().tobytes()) == rec["frame_bg"], f"env-0 frame step {k}"
         if "render_packed" in rec:
             assert _sha(o.render_packed().tobytes()) == rec["render_packed"], f"packed render step {k}"
             assert _sha(o.render_shades().tobytes()) == rec["render_shades"], f"shade render step {k}"
