@@ -490,6 +490,40 @@ class GbxVecCudaBackend:
         self._torch().cuda.synchronize(self._ordinal)
         return self._view("i32")[0].cpu().numpy().copy()
 
+    # ------------------------------------------------------------------ PyBoy state files
+    def save_state(self, env_idx: int = 0):
+        """Env ``env_idx`` as a ``PyBoyState`` (warp_vec.py:1024-1033)."""
+        from .state_io import state_from_backend
+
+        self._check_env(env_idx)
+        return state_from_backend(self, env_idx)
+
+    def save_state_file(self, path: str, env_idx: int = 0) -> None:
+        """Write env ``env_idx`` as a PyBoy version-9 state file (warp_vec.py:1035-1044)."""
+        from .state_io import save_pyboy_state
+
+        save_pyboy_state(self.save_state(env_idx), path)
+
+    def load_state(self, state, env_idx: int = 0) -> None:
+        """Load a ``PyBoyState`` into env ``env_idx`` (warp_vec.py:1046-1055)."""
+        from .state_io import apply_state_to_backend
+
+        self._check_env(env_idx)
+        apply_state_to_backend(state, self, env_idx)
+
+    def load_state_file(self, path: str, env_idx: int = 0) -> None:
+        """Load a PyBoy state file (versions 9-15) into env ``env_idx`` (warp_vec.py:1057-1074)."""
+        from .state_io import load_pyboy_state
+
+        self._need()
+        state = load_pyboy_state(path, expected_cart_ram_size=int(self._spec.ram_byte_length))
+        self.load_state(state, env_idx)
+
+    def _check_env(self, env_idx: int) -> None:
+        self._need()
+        if env_idx < 0 or env_idx >= self.num_envs:
+            raise ValueError(f"env_idx {env_idx} out of range [0, {self.num_envs})")
+
     def read_frame_bg_shade_env0(self) -> bytes:
         """Env 0's 160x144 frame, row-major, one shade per byte (warp_vec.py:1389-1404).
 

@@ -298,3 +298,39 @@ def test_force_lcdc_on_render_matches_oracle():
             assert np.array_equal(be.pixels_packed_torch().cpu().numpy(), o.render_packed()), f"render {k}"
     finally:
         be.close()
+
+
+@pytest.mark.parametrize("name", ["cfg2", "cfg4"])
+def test_state_files_match_reference_on_gpu(name, tmp_path):
+    """save_state_file writes the reference's bytes for the same state, and
+    load_state_file puts a reference-saved file into an env exactly as the
+    reference does (then stepping stays in parity)."""
+    import json
+
+    from tests.conftest import GOLDEN
+
+    gold = json.loads((GOLDEN / "state_io.json").read_text())["cases"][name]
+    blob = np.load(GOLDEN / "state_io.npz")[f"saved_{name}"].tobytes()
+    rom = roms.CONFIG_ROMS[gold["config"]]()
+    n = gold["num_envs"]
+    be = _backend(rom, n, 24, 8)
+    try:
+        for a in gold["actions"]:
+            _step(be, a)
+        assert st.digest(be.export_state()) == gold["source_digest"]
+        p = tmp_path / "s.state"
+        be.save_state_file(str(p), env_idx=gold["env"])
+        assert p.read_bytes() == blob
+    finally:
+        be.close()
+    be = _backend(rom, n, 24, 8)
+    try:
+        p = tmp_path / "ref.state"
+        p.write_bytes(blob)
+        be.load_state_file(str(p), env_idx=0)
+        assert st.digest(be.export_state()) == gold["applied_digest"]
+        for rec in gold["after"]:
+            _step(be, rec["actions"])
+            assert st.digest(be.export_state()) == rec["digest"]
+    finally:
+        be.close()
