@@ -288,6 +288,74 @@ def run_gbx(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_rollout_workload(args) -> None:
+    """policy rollouts on the MBC3 + PPU cartridge.
+
+    Per env-step: packed render -> 2 bpp unpack -> bf16 conv policy -> sampled
+    actions -> step_torch -> masked restore of a seeded 5 % of envs from a
+    snapshot taken after warm-up. Timed end to end with CUDA events; the
+    policy and the restores are inside the timed region.
+    """
+    import torch
+
+    from gbxcule_b200 import GbxVecCudaBackend, ResetCache, roms
+    from gbxcule_b200.multi import job_rate, rank_seed, reduce_run_stats
+    from gbxcule_b200.rollout import make_policy, run_rollout
+
+    ws, rank, local = _dist()
+    dist = None
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    n = args.envs or 131072
+    K, W = args.steps, args.warmup
+    be = GbxVecCudaBackend(roms.config5_rom(), num_envs=n, frames_per_step=FRAMES,
+                           release_after_frames=RELEASE, render_on_step=False, device=f"cuda:{local}")
+    be.reset()
+    pol = make_policy(dev, seed=rank_seed(5, rank))
+    gen = torch.Generator(device=dev).manual_seed(rank_seed(1005, rank))
+    packed = torch.empty((n, 72, 20), dtype=torch.uint8, device=dev)
+    run_rollout(be, pol, W, generator=gen, packed_out=packed)
+    cache = ResetCache.from_backend(be, env_idx=0)
+    masks = [torch.as_tensor(np.random.default_rng(rank_seed(2005, rank) + k).random(n) < 0.05, device=dev)
+             for k in range(K)]
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    run_rollout(be, pol, K, generator=gen, reset_cache=cache, reset_mask=lambda k: masks[k], packed_out=packed)
+    e1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    (ms,), _ = reduce_run_stats(dist, dev, [e0.elapsed_time(e1)], [])
+    cache.close()
+    be.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = job_rate(n, ws, K, ms)
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u8", "data": "synthetic",
+        "config": {"workload": f"config5: MBC3 + PPU cartridge, {n} envs/GPU, frameskip 24, bf16 conv policy "
+                               "on packed frames, sampled actions, 5 % masked restores per step",
+                   "envs_per_gpu": n, "policy": "Conv(1-32,k4,s2)-Conv(32-64,k3,s2)-Conv(64-64,k3,s1)-"
+                   "Linear(512)-Linear(9), bf16, random init"},
+        "emulated_frames_per_s": value * FRAMES, "clocks": clk}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -295,11 +363,16 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="gbx", choices=["gbx", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config2", choices=["config2", "config5"],
+                    help="config2 (default): the benchmark line; config5: policy rollouts")
+    ap.add_argument("--envs", type=int, default=0, help="envs per GPU for --workload config5")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "config5":
+        run_rollout_workload(args)
     else:
         run_gbx(args)
 

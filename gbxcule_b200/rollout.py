@@ -1,0 +1,124 @@
+"""Policy rollouts on packed observations (the reference's RL loop shape).
+
+The reference's RL loops (``src/gbxcule/rl/``) render packed 2 bpp frames,
+unpack them with a 256 x 4 lookup table (``rl/packed_pixels.py:26-71``), run
+a torch policy on them, sample one action per env and call ``step_torch``;
+finished episodes are restored from a ``ResetCache``. This module is that
+loop over ``GbxVecCudaBackend``: frames go from libgbx's packed buffer to the
+policy without leaving the GPU, and every tensor stays on the backend's
+device and current stream.
+
+``PixelPolicy`` is BASELINE's config-5 network: bf16
+Conv(1->32, k4, s2) -> Conv(32->64, k3, s2) -> Conv(64->64, k3, s1) ->
+Linear(., 512) -> Linear(512, 9) with ReLUs, on frames scaled by 1/3 (the
+strides are not given by the benchmark; 2/2/1 are used).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any, Callable
+
+_LUT: dict[str, Any] = {}
+
+
+def unpack_lut(device) -> Any:
+    """[256, 4] uint8: byte -> its four 2-bit pixels, first pixel in bits 0-1."""
+    import torch
+
+    key = str(device)
+    if key not in _LUT:
+        v = torch.arange(256, dtype=torch.int32)
+        _LUT[key] = torch.stack([(v >> s) & 3 for s in (0, 2, 4, 6)], dim=1).to(torch.uint8).to(device)
+    return _LUT[key]
+
+
+def unpack_2bpp_u8(packed) -> Any:
+    """Unpack uint8 2 bpp bytes along the last axis (rl/packed_pixels.py:62-71)."""
+    import torch
+
+    if packed.dtype is not torch.uint8:
+        raise ValueError("packed_u8 must be uint8")
+    out = unpack_lut(packed.device)[packed.to(torch.int64)]
+    return out.reshape(*packed.shape[:-1], packed.shape[-1] * 4)
+
+
+def pack_2bpp_u8(pixels) -> Any:
+    """Pack uint8 pixels (0..3) four per byte along the last axis (rl/packed_pixels.py:47-59)."""
+    import torch
+
+    if pixels.dtype is not torch.uint8:
+        raise ValueError("unpacked_u8 must be uint8")
+    if pixels.shape[-1] % 4:
+        raise ValueError("last dimension must be divisible by 4")
+    q = pixels.reshape(*pixels.shape[:-1], pixels.shape[-1] // 4, 4)
+    return q[..., 0] | (q[..., 1] << 2) | (q[..., 2] << 4) | (q[..., 3] << 6)
+
+
+def _policy_class():
+    import torch
+    from torch import nn
+
+    class PixelPolicy(nn.Module):
+        def __init__(self, num_actions: int = 9) -> None:
+            super().__init__()
+            self.conv = nn.Sequential(
+                nn.Conv2d(1, 32, 4, stride=2), nn.ReLU(),
+                nn.Conv2d(32, 64, 3, stride=2), nn.ReLU(),
+                nn.Conv2d(64, 64, 3, stride=1), nn.ReLU(), nn.Flatten())
+            with torch.no_grad():
+                flat = self.conv(torch.zeros(1, 1, 72, 80)).shape[1]
+            self.head = nn.Sequential(nn.Linear(flat, 512), nn.ReLU(), nn.Linear(512, num_actions))
+
+        def forward(self, frames_u8):  # [B, 72, 80] uint8 shades
+            x = frames_u8.unsqueeze(1).to(self.head[0].weight.dtype) / 3.0
+            return self.head(self.conv(x))
+
+    return PixelPolicy
+
+
+def make_policy(device, *, num_actions: int = 9, seed: int = 0, dtype=None):
+    """Random-init config-5 policy in bf16 on ``device``."""
+    import torch
+
+    torch.manual_seed(seed)
+    pol = _policy_class()(num_actions).to(device=device, dtype=dtype or torch.bfloat16)
+    return pol.eval()
+
+
+@dataclass
+class Rollout:
+    actions: list = field(default_factory=list)   # int32 [N] per step (device tensors)
+    resets: list = field(default_factory=list)    # bool [N] per step, or None
+
+
+def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 16384,
+                reset_cache=None, reset_mask: Callable[[int], Any] | None = None,
+                packed_out=None) -> Rollout:
+    """``steps`` env-steps of render -> unpack -> policy -> sample -> step.
+
+    ``reset_mask(k)`` (a CUDA bool [N] or None) selects envs restored from
+    ``reset_cache`` after step k. The policy runs in chunks of ``chunk`` envs
+    to bound activation memory. Returns the sampled actions (and masks).
+    """
+    import torch
+
+    n = backend.num_envs
+    dev = torch.device("cuda", backend._ordinal)
+    packed = packed_out if packed_out is not None else torch.empty((n, 72, 20), dtype=torch.uint8, device=dev)
+    out = Rollout()
+    with torch.no_grad():
+        for k in range(steps):
+            backend.render_pixels_snapshot_packed_to_torch(packed)
+            acts = torch.empty(n, dtype=torch.int32, device=dev)
+            for lo in range(0, n, chunk):
+                hi = min(n, lo + chunk)
+                logits = policy(unpack_2bpp_u8(packed[lo:hi])).float()
+                acts[lo:hi] = torch.multinomial(torch.softmax(logits, dim=-1), 1, generator=generator)[:, 0].to(torch.int32)
+            backend.step_torch(acts)
+            out.actions.append(acts)
+            mask = reset_mask(k) if reset_mask is not None else None
+            if mask is not None and reset_cache is not None:
+                reset_cache.apply_mask_torch(mask)
+            out.resets.append(mask)
+    return out

@@ -334,3 +334,42 @@ def test_state_files_match_reference_on_gpu(name, tmp_path):
             assert st.digest(be.export_state()) == rec["digest"]
     finally:
         be.close()
+
+
+def test_policy_rollout_with_resets_replays_on_oracle():
+    """Config-5 rollout shape: packed frames -> bf16 policy -> sampled actions
+    -> step_torch, with masked restores from a ResetCache; the recorded
+    actions and masks replayed on the oracle give the same state and frames."""
+    from gbxcule_b200 import ResetCache, rollout
+
+    rom = roms.config5_rom()
+    n = 48
+    be = _backend(rom, n, 24, 8, render_pixels_packed=True, render_on_step=False)
+    o = OracleEnvs(rom, roms.boot_stub(), n)
+    try:
+        a0 = roms.uniform_actions(np.random.default_rng(5), n)
+        _step(be, a0)
+        o.step(a0, 24, 8)
+        cache = ResetCache.from_backend(be, env_idx=0)
+        snap = o.snapshot(0)
+        pol = rollout.make_policy("cuda")
+        gen = torch.Generator(device="cuda").manual_seed(11)
+        masks = [torch.as_tensor(np.random.default_rng(60 + k).random(n) < 0.25, device="cuda") for k in range(4)]
+        frames = []
+        orig = be.render_pixels_snapshot_packed_to_torch
+
+        def rec(out, base_offset_bytes=0):
+            orig(out, base_offset_bytes)
+            frames.append(out.clone())
+
+        be.render_pixels_snapshot_packed_to_torch = rec
+        ro = rollout.run_rollout(be, pol, 4, generator=gen, reset_cache=cache, reset_mask=lambda k: masks[k])
+        for k in range(4):
+            assert np.array_equal(frames[k].cpu().numpy(), o.render_packed()), f"policy input {k}"
+            a = ro.actions[k].cpu().numpy()
+            assert a.min() >= 0 and a.max() < 9
+            o.step(a, 24, 8)
+            o.restore(snap, masks[k].cpu().numpy().astype(np.uint8))
+        assert not st.diff(be.export_state(), o.state(), n)
+    finally:
+        be.close()
