@@ -61,7 +61,12 @@ STEP_STATE_BYTES = 2 * (27 * 4 + 2 * 8 + 3 + 20 * 4 + 12) + 4 + 32 * 4
 # `bench.py --steps 3 --warmup 3 --no-cpu-baseline`. It includes the
 # emulated programs' RAM lines and the write-back of the L2 flush buffer
 # written just before the launch.
-STEP_KERNEL_DRAM_BYTES_4096 = 75.305728e6 + 345.320448e6
+STEP_KERNEL_DRAM_BYTES_4096 = 76.654080e6 + 336.493056e6
+# smsp__inst_executed.sum / emulated SM83 instructions of one step-kernel
+# launch on this workload, from the same ncu capture: the integer-issue cost
+# of one emulated instruction, used for the issue roofline below.
+WARP_INSTR_PER_EMULATED_INSTR = 61.636727523e9 / (4096 * 197327.3)
+SMS, ISSUE_PER_SM_PER_CLOCK = 148, 4
 
 
 def _peaks() -> dict:
@@ -130,6 +135,15 @@ def _dist():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return ws, rank, local
+
+
+def _issue_roofline(emu_instr_per_s_per_gpu: float, clk: dict) -> dict:
+    mhz = clk.get("sm_mhz") or 1965.0
+    peak = SMS * ISSUE_PER_SM_PER_CLOCK * mhz * 1e6
+    achieved = emu_instr_per_s_per_gpu * WARP_INSTR_PER_EMULATED_INSTR
+    return {"bound": "integer issue", "achieved": achieved, "peak": peak, "unit": "warp-instructions/s per GPU",
+            "frac": achieved / peak, "warp_instr_per_emulated_instr": WARP_INSTR_PER_EMULATED_INSTR,
+            "note": "warp instructions per emulated instruction from an ncu capture of this workload"}
 
 
 def cpu_oracle_rate(total_envs_hint: int, warmup: int, steps: int, threads: int, seed: int = 0) -> dict:
@@ -279,6 +293,10 @@ def run_gbx(args) -> None:
                      "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
                      "peak_source": peaks["source"], "kernel": "gb_step_kernel",
                      "kernel_ms": step_avg_ms, "bytes_per_env_step": STEP_STATE_BYTES},
+        # the binding roof: warp-instruction issue slots used by the step
+        # kernel (emulated instructions/s x warp instructions per emulated
+        # instruction) over the SMs' issue slots at the sampled SM clock
+        "issue_roofline": _issue_roofline(ninstr / (step_avg_ms * K / 1e3) / ws, clk),
         "clocks": clk,
         "gpu_launches": 2 * K,
         "wall_s_timed": wall,
