@@ -253,6 +253,7 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
   }
   st.rom = rom_d;
   st.boot = boot_d;
+  st.pix = h->pix;
   if ((rc = dalloc(&h->frame_bg, (size_t)160 * SCREEN_H)) || (rc = dalloc(&h->pre, (size_t)rom_bytes))) {
     free_env(h);
     delete h;
@@ -360,8 +361,9 @@ int gbx_snapshot_create(gbx_env* h, int32_t env_idx, void* stream, gbx_snapshot*
   DeviceGuard g(h->cfg.device);
   gbx_snapshot* sn = new (std::nothrow) gbx_snapshot();
   if (!sn) return fail(GBX_ERR_OOM, "host allocation failed");
-  const size_t bytes = (size_t)MEM_SIZE + h->ram_rows + SERIAL_MAX + 4 * CS_STRIDE + 4 * I32_COUNT + 8 * I64_COUNT +
-                       U8_COUNT + 64;
+  const size_t pix_bytes = h->pix ? (size_t)SHADE_BYTES : 0;
+  const size_t bytes = (size_t)MEM_SIZE + h->ram_rows + SERIAL_MAX + pix_bytes + 4 * CS_STRIDE + 4 * I32_COUNT +
+                       8 * I64_COUNT + U8_COUNT + 64;
   cudaError_t e = cudaMalloc(&sn->block, bytes);
   if (e != cudaSuccess) {
     delete sn;
@@ -372,6 +374,7 @@ int gbx_snapshot_create(gbx_env* h, int32_t env_idx, void* stream, gbx_snapshot*
   uint8_t* p = static_cast<uint8_t*>(sn->block);
   sn->s.mem = p; p += MEM_SIZE;
   sn->s.serial = p; p += SERIAL_MAX;
+  sn->s.pix = h->pix ? p : nullptr; p += pix_bytes;  // 5760: keeps 16-byte alignment
   sn->s.cart_ram = p; p += (h->ram_rows + 15) & ~15;
   sn->s.i64 = reinterpret_cast<int64_t*>(p); p += 8 * I64_COUNT;
   sn->s.cart_state = reinterpret_cast<int32_t*>(p); p += 4 * CS_STRIDE;

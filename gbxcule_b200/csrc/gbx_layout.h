@@ -86,6 +86,7 @@ struct DevState {
   float* obs;
   float* reward;
   uint32_t* status;
+  uint8_t* pix;           // [N][72*80] shade buffer, or null (render_pixels=False)
 };
 
 // Debug traps of the reference kernel (cpu_step_builder.py:1320-1393,
@@ -107,6 +108,7 @@ struct Snapshot {
   int32_t* i32;         // [I32_COUNT]
   int64_t* i64;         // [I64_COUNT]
   uint8_t* u8s;         // [U8_COUNT]
+  uint8_t* pix;         // [72*80] shade image, or null when the batch has no shade buffer
   int32_t ram_bytes;
 };
 

@@ -5,15 +5,18 @@
 // reset_copy_{strided,scalar}_* (src/gbxcule/kernels/reset_mask.py:12-79,
 // driven by src/gbxcule/core/reset_cache.py:192-307) with one launch. It
 // restores exactly the fields ResetCache restores: the 64 KiB address space,
-// cart_state, cart RAM, the serial buffer and every per-env scalar, including
-// the host-path action buffer; env-0 latches, obs and reward are untouched.
+// cart_state, cart RAM, the serial buffer, the 72x80 shade image when the
+// batch has one (reset_cache.py:111-112,237-244) and every per-env scalar,
+// including the host-path action buffer; env-0 latches, obs, reward and the
+// packed image are untouched.
 //
 // With env-major byte arrays a restored env is three contiguous blocks
 // (64 KiB + cart RAM + 1 KiB), so the restore is a streaming copy: a grid of
-// persistent blocks walks the envs, every block reads one mask byte per env
-// and a masked env is copied by one whole block with 16-byte loads and
-// stores. The snapshot source stays resident in L2, so HBM sees the writes
-// only (plus one read of the snapshot).
+// persistent blocks shares out the envs, each block reads the mask bytes of
+// up to 256 of its envs at once, lists the masked ones, and copies each with
+// the whole block, four 16-byte loads in flight per thread. The snapshot
+// source stays resident in L2, so HBM sees the writes only (plus one read of
+// the snapshot).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -50,9 +53,15 @@ __global__ void init_kernel(DevState st) {
 __device__ __forceinline__ void block_copy(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src,
                                            int bytes) {
   if (((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src) | (uintptr_t)bytes) & 15) == 0) {
-    uint4* d = reinterpret_cast<uint4*>(dst);
-    const uint4* s = reinterpret_cast<const uint4*>(src);
-    for (int k = threadIdx.x; k < bytes / 16; k += blockDim.x) d[k] = s[k];
+    uint4* __restrict__ d = reinterpret_cast<uint4*>(dst);
+    const uint4* __restrict__ s = reinterpret_cast<const uint4*>(src);
+    const int n16 = bytes / 16, step = blockDim.x;
+    int k = threadIdx.x;
+    for (; k + 3 * step < n16; k += 4 * step) {  // four loads in flight before the stores
+      const uint4 a = s[k], b = s[k + step], c = s[k + 2 * step], e = s[k + 3 * step];
+      d[k] = a; d[k + step] = b; d[k + 2 * step] = c; d[k + 3 * step] = e;
+    }
+    for (; k < n16; k += step) d[k] = s[k];
   } else {
     for (int k = threadIdx.x; k < bytes; k += blockDim.x) dst[k] = src[k];
   }
@@ -64,6 +73,7 @@ __global__ void snapshot_kernel(DevState st, Snapshot snap, int env) {
   block_copy(snap.mem, st.mem + (size_t)env * MEM_SIZE, MEM_SIZE);
   block_copy(snap.cart_ram, st.cart_ram + (size_t)env * st.ram_rows, snap.ram_bytes);
   block_copy(snap.serial, st.serial + (size_t)env * SERIAL_MAX, SERIAL_MAX);
+  if (snap.pix && st.pix) block_copy(snap.pix, st.pix + (size_t)env * SHADE_BYTES, SHADE_BYTES);
   const int t = threadIdx.x;
   if (t < CS_STRIDE) snap.cart_state[t] = st.cart_state[(size_t)t * S + env];
   if (t < I32_COUNT) snap.i32[t] = st.i32[(size_t)t * S + env];
@@ -75,16 +85,30 @@ __global__ void snapshot_kernel(DevState st, Snapshot snap, int env) {
 __global__ void __launch_bounds__(RESTORE_THREADS) restore_kernel(DevState st, Snapshot snap,
                                                                   const uint8_t* __restrict__ mask) {
   const size_t S = (size_t)st.S;
-  for (int e = blockIdx.x; e < st.n; e += gridDim.x) {
-    if (!mask[e]) continue;  // block-uniform
-    block_copy(st.mem + (size_t)e * MEM_SIZE, snap.mem, MEM_SIZE);
-    block_copy(st.cart_ram + (size_t)e * st.ram_rows, snap.cart_ram, snap.ram_bytes);
-    block_copy(st.serial + (size_t)e * SERIAL_MAX, snap.serial, SERIAL_MAX);
-    const int t = threadIdx.x;
-    if (t < CS_STRIDE) st.cart_state[(size_t)t * S + e] = snap.cart_state[t];
-    if (t < I32_COUNT) st.i32[(size_t)t * S + e] = snap.i32[t];
-    if (t < I64_COUNT) st.i64[(size_t)t * S + e] = snap.i64[t];
-    if (t < U8_COUNT) st.u8s[(size_t)t * S + e] = snap.u8s[t];
+  // this block's envs are blockIdx.x + j * gridDim.x; read their mask bytes
+  // at once and list the masked ones
+  __shared__ int list[RESTORE_THREADS];
+  __shared__ int count;
+  for (int j0 = 0; blockIdx.x + j0 * gridDim.x < st.n; j0 += RESTORE_THREADS) {
+    if (threadIdx.x == 0) count = 0;
+    __syncthreads();
+    const int e_t = blockIdx.x + (j0 + threadIdx.x) * gridDim.x;
+    if (e_t < st.n && mask[e_t]) list[atomicAdd(&count, 1)] = e_t;
+    __syncthreads();
+    const int cnt = count;
+    for (int q = 0; q < cnt; q++) {
+      const int e = list[q];
+      block_copy(st.mem + (size_t)e * MEM_SIZE, snap.mem, MEM_SIZE);
+      block_copy(st.cart_ram + (size_t)e * st.ram_rows, snap.cart_ram, snap.ram_bytes);
+      block_copy(st.serial + (size_t)e * SERIAL_MAX, snap.serial, SERIAL_MAX);
+      if (snap.pix && st.pix) block_copy(st.pix + (size_t)e * SHADE_BYTES, snap.pix, SHADE_BYTES);
+      const int t = threadIdx.x;
+      if (t < CS_STRIDE) st.cart_state[(size_t)t * S + e] = snap.cart_state[t];
+      if (t < I32_COUNT) st.i32[(size_t)t * S + e] = snap.i32[t];
+      if (t < I64_COUNT) st.i64[(size_t)t * S + e] = snap.i64[t];
+      if (t < U8_COUNT) st.u8s[(size_t)t * S + e] = snap.u8s[t];
+    }
+    __syncthreads();  // list and count are reused by the next batch
   }
 }
 
