@@ -12,9 +12,11 @@
 //
 // Mapping: one 128-thread block per env. The env's VRAM (8 KiB), OAM and LCD
 // registers are staged in shared memory with 16-byte coalesced loads (every
-// byte the renderer can touch lies in them), each output row builds its
-// sprite line list once, and the output image is staged in shared memory so
-// the global store is contiguous 16-byte chunks. HBM traffic per env is the
+// byte the renderer can touch lies in them). Each output row first resolves
+// its sprites into a line of 80 sampled positions (at most 10 sprites x 4
+// samples), so a pixel costs one BG fetch and one line read instead of a
+// scan of the row's sprites. The image is staged in shared memory so the
+// global store is contiguous 16-byte chunks. HBM traffic per env is the
 // staged 8.4 KiB read plus the image write.
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -35,8 +37,9 @@ __global__ void __launch_bounds__(RENDER_THREADS) render_kernel(DevState st, uin
   __shared__ __align__(16) uint8_t vram[0x2000];
   __shared__ __align__(16) uint8_t oam[160];
   __shared__ __align__(16) uint8_t io[16];            // FF40-FF4F
-  __shared__ uint32_t spr[OUT_ROWS][MAX_SPR];          // left+8 | lo<<8 | hi<<16 | attr<<24
-  __shared__ uint8_t nspr_s[OUT_ROWS];
+  // winning sprite pixel of each sampled position: left+8 | colour << 8 |
+  // palette << 10 | BG priority << 11, 0 = none
+  __shared__ __align__(16) uint16_t line[OUT_ROWS][80];
   __shared__ __align__(16) uint8_t img[ENV_BYTES];
 
   const int env = blockIdx.x;
@@ -50,45 +53,60 @@ __global__ void __launch_bounds__(RENDER_THREADS) render_kernel(DevState st, uin
     if (t < 10) reinterpret_cast<uint4*>(oam)[t] = reinterpret_cast<const uint4*>(m + 0xFE00)[t];
     if (t == 10) *reinterpret_cast<uint4*>(io) = *reinterpret_cast<const uint4*>(m + 0xFF40);
   }
+  {
+    uint4* l4 = reinterpret_cast<uint4*>(&line[0][0]);
+    for (int k = t; k < (int)(sizeof(line) / 16); k += RENDER_THREADS) l4[k] = make_uint4(0, 0, 0, 0);
+  }
   __syncthreads();
   const int lcdc = io[0x0], scy = io[0x2], scx = io[0x3], bgp = io[0x7];
   const int obp0 = io[0x8], obp1 = io[0x9], wy = io[0xA], wx = io[0xB];
   const int sh = (lcdc & 4) ? 16 : 8;
 
-  // sprite line list of each output row (first 10 in OAM order)
+  // sprite line of each output row y = 2*oy: the row's first 10 sprites in
+  // OAM order (the count ignores X); at each sampled x (even) the opaque
+  // pixel of the sprite with the smallest X wins, ties to the lower OAM index
   if (t < OUT_ROWS) {
-    const int y = t * 2;
-    int nspr = 0;
+    uint16_t* L = line[t];
     if (lcdc & 2) {
+      const int y = t * 2;
+      int nspr = 0;
       for (int s = 0; s < 40 && nspr < MAX_SPR; s++) {
         const int sy = oam[4 * s], sx = oam[4 * s + 1];
         if (sx == 0 || sy == 0 || sx >= 168 || sy >= 160) continue;
         const int top = sy - 16;
         if (y < top || y >= top + sh) continue;
+        nspr++;
         int tile = oam[4 * s + 2];
         const int attr = oam[4 * s + 3];
         int row = y - top;
         if ((attr >> 6) & 1) row = sh - 1 - row;
         if (sh == 16) { tile &= 0xFE; if (row >= 8) { tile++; row -= 8; } }
-        const int ta = tile * 16 + row * 2;  // VRAM offset of 0x8000 + tile*16 + row*2
-        spr[t][nspr] = (uint32_t)sx | ((uint32_t)vram[ta] << 8) | ((uint32_t)vram[ta + 1] << 16) |
-                       ((uint32_t)attr << 24);
-        nspr++;
+        const int lo = vram[tile * 16 + row * 2], hi = vram[tile * 16 + row * 2 + 1];
+        const int left = sx - 8;
+        for (int x = left + (left & 1); x < left + 8; x += 2) {  // the four even x the sprite covers
+          if (x < 0 || x >= 160) continue;
+          const int pxo = x - left;
+          const int bit = ((attr >> 5) & 1) ? pxo : 7 - pxo;
+          const int color = (((hi >> bit) & 1) << 1) | ((lo >> bit) & 1);
+          if (color == 0) continue;
+          const int cur = L[x >> 1];
+          if (cur == 0 || left < (cur & 0xFF) - 8)
+            L[x >> 1] = (uint16_t)((left + 8) | (color << 8) | (((attr >> 4) & 1) << 10) | (((attr >> 7) & 1) << 11));
+        }
       }
     }
-    nspr_s[t] = (uint8_t)nspr;
   }
   __syncthreads();
 
   for (int i = t; i < ENV_BYTES; i += RENDER_THREADS) {
     const int oy = i / BPR, ob = i - oy * BPR;
     const int y = oy * 2;
-    const int nspr = nspr_s[oy];
     const bool win_row = (lcdc & 0x20) && y >= wy;
     int packed = 0;
 #pragma unroll
     for (int k = 0; k < (PACKED ? 4 : 1); k++) {
-      const int x = PACKED ? (ob * 4 + k) * 2 : ob * 2;
+      const int ox = PACKED ? ob * 4 + k : ob;
+      const int x = ox * 2;
       int shade = 0, bg_color = 0;
       if (lcdc & 1) {
         int px, py, map;
@@ -104,23 +122,11 @@ __global__ void __launch_bounds__(RENDER_THREADS) render_kernel(DevState st, uin
         bg_color = (((vram[ta + 1] >> bit) & 1) << 1) | ((vram[ta] >> bit) & 1);
         shade = (bgp >> (bg_color * 2)) & 3;
       }
-      if (nspr) {
-        int best_left = 1 << 30, best_color = 0, best_attr = 0;
-        for (int j = 0; j < nspr; j++) {
-          const uint32_t e = spr[oy][j];
-          const int left = (int)(e & 0xFF) - 8;
-          if (x < left || x >= left + 8 || left >= best_left) continue;
-          const int attr = e >> 24, lo = (e >> 8) & 0xFF, hi = (e >> 16) & 0xFF;
-          const int pxo = x - left;
-          const int bit = ((attr >> 5) & 1) ? pxo : 7 - pxo;
-          const int color = (((hi >> bit) & 1) << 1) | ((lo >> bit) & 1);
-          if (color == 0) continue;
-          best_left = left; best_color = color; best_attr = attr;
-        }
-        if (best_color && !(((best_attr >> 7) & 1) && bg_color != 0)) {
-          const int pal = ((best_attr >> 4) & 1) ? obp1 : obp0;
-          shade = (pal >> (best_color * 2)) & 3;
-        }
+      const int e = line[oy][ox];
+      if (e) {
+        const int color = (e >> 8) & 3;
+        if (!(((e >> 11) & 1) && bg_color != 0))
+          shade = ((((e >> 10) & 1) ? obp1 : obp0) >> (color * 2)) & 3;
       }
       packed |= (shade & 3) << (2 * k);
     }
