@@ -52,49 +52,53 @@ namespace gbx {
 enum Family : uint8_t {
   FM_LDRR, FM_LD16, FM_ST_A, FM_LD_A, FM_INCDEC16, FM_INCDEC8, FM_INCDEC_HL, FM_LD8_IMM,
   FM_ST_HL_IMM, FM_ROTA, FM_ST_SP16, FM_ADDHL, FM_TRAP, FM_JR, FM_DAA, FM_FLAGOP,
-  FM_LDR_HL, FM_STHL_R, FM_HALT, FM_ALU_R, FM_ALU_V, FM_RET, FM_POP, FM_JP,
-  FM_CALL, FM_PUSH, FM_RST, FM_CB, FM_SPADD, FM_IME
+  FM_LDR_HL, FM_STHL_R, FM_HALT, FM_ALU_V, FM_RET, FM_POP, FM_JP,
+  FM_CALL, FM_PUSH, FM_RST, FM_CB_HL, FM_SPADD, FM_IME,
+  // register-operand forms split by operation, so their cases hold no inner dispatch
+  FM_CB_ROT, FM_CB_BIT, FM_CB_RES, FM_CB_SET, FM_ALU_ADC, FM_ALU_SBC, FM_ALU_LOG
 };
-enum ReadMode : uint8_t { RD_NONE, RD_HL, RD_BC, RD_DE, RD_A16, RD_FF_N, RD_FF_C, RD_SP };
 
-// entry = family | read_mode << 5 (CB-prefixed (HL) forms are fixed up from the CB byte)
+// CB-prefixed instructions take their family from the second byte
+__host__ __device__ constexpr uint8_t cb_family(int b1) {
+  return (b1 & 7) == 6 ? FM_CB_HL : (uint8_t)(FM_CB_ROT + (b1 >> 6));
+}
+
+// family of an unprefixed opcode (0xCB: see cb_family)
 __host__ __device__ constexpr uint8_t decode_entry(int op) {
   int x = op >> 6, y = (op >> 3) & 7, z = op & 7;
-  if (op == 0xCB) return FM_CB;
+  if (op == 0xCB) return FM_CB_HL;
   if (op == 0x10 || op == 0xD3 || op == 0xDB || op == 0xDD || op == 0xE3 || op == 0xE4 ||
       op == 0xEB || op == 0xEC || op == 0xED || op == 0xF4 || op == 0xFC || op == 0xFD)
     return FM_TRAP;
   if (x == 1) {
     if (op == 0x76) return FM_HALT;
-    if (z == 6) return FM_LDR_HL | (RD_HL << 5);
+    if (z == 6) return FM_LDR_HL;
     if (y == 6) return FM_STHL_R;
     return FM_LDRR;
   }
-  if (x == 2) return z == 6 ? (FM_ALU_V | (RD_HL << 5)) : FM_ALU_R;
+  if (x == 2) return z == 6 ? FM_ALU_V : y < 2 ? FM_ALU_ADC : (y < 4 || y == 7) ? FM_ALU_SBC : FM_ALU_LOG;
   if (x == 0) {
     switch (z) {
       case 0: return op == 0x00 ? FM_LDRR : op == 0x08 ? FM_ST_SP16 : FM_JR;
       case 1: return (y & 1) ? FM_ADDHL : FM_LD16;
       case 2:
-        if (y & 1) return FM_LD_A | ((op == 0x0A ? RD_BC : op == 0x1A ? RD_DE : RD_HL) << 5);
+        if (y & 1) return FM_LD_A;
         return FM_ST_A;
       case 3: return FM_INCDEC16;
-      case 4: case 5: return y == 6 ? (FM_INCDEC_HL | (RD_HL << 5)) : FM_INCDEC8;
+      case 4: case 5: return y == 6 ? FM_INCDEC_HL : FM_INCDEC8;
       case 6: return y == 6 ? FM_ST_HL_IMM : FM_LD8_IMM;
       default: return y == 4 ? FM_DAA : y >= 5 ? FM_FLAGOP : FM_ROTA;
     }
   }
   switch (op) {  // x == 3
     case 0xC0: case 0xC8: case 0xD0: case 0xD8: case 0xC9: case 0xD9:
-      return FM_RET | (RD_SP << 5);
-    case 0xC1: case 0xD1: case 0xE1: case 0xF1: return FM_POP | (RD_SP << 5);
+      return FM_RET;
+    case 0xC1: case 0xD1: case 0xE1: case 0xF1: return FM_POP;
     case 0xC2: case 0xCA: case 0xD2: case 0xDA: case 0xC3: case 0xE9: return FM_JP;
     case 0xC4: case 0xCC: case 0xD4: case 0xDC: case 0xCD: return FM_CALL;
     case 0xC5: case 0xD5: case 0xE5: case 0xF5: return FM_PUSH;
     case 0xE0: case 0xE2: case 0xEA: return FM_ST_A;
-    case 0xF0: return FM_LD_A | (RD_FF_N << 5);
-    case 0xF2: return FM_LD_A | (RD_FF_C << 5);
-    case 0xFA: return FM_LD_A | (RD_A16 << 5);
+    case 0xF0: case 0xF2: case 0xFA: return FM_LD_A;
     case 0xE8: case 0xF8: case 0xF9: return FM_SPADD;
     case 0xF3: case 0xFB: return FM_IME;
     default: break;
@@ -105,8 +109,7 @@ __host__ __device__ constexpr uint8_t decode_entry(int op) {
 
 // 32-bit decoded instruction: opcode | imm16 << 8 | entry << 24
 __host__ __device__ constexpr uint32_t decode_word(int op, int b1, int b2) {
-  uint32_t e = decode_entry(op);
-  if (op == 0xCB && (b1 & 7) == 6) e |= RD_HL << 5;
+  const uint32_t e = op == 0xCB ? cb_family(b1) : decode_entry(op);
   return (uint32_t)op | ((uint32_t)b1 << 8) | ((uint32_t)b2 << 16) | (e << 24);
 }
 
@@ -140,6 +143,20 @@ enum Event { EV_FIRST = 1, EV_HALT = 2, EV_TRAP = 4, EV_LCDC = 8, EV_PPU = 16, E
 // CPU registers and the event clock: the only state the interpreter loop
 // keeps in registers. Everything else lives in Emu, in local memory, and is
 // touched by the out-of-line slow paths only.
+// RLC RRC RL RR SLA SRA SWAP SRL of v (bitops.py); oc = carry in, c = carry out
+__device__ __forceinline__ int cb_rot(int kind, int v, int oc, int& c) {
+  switch (kind) {
+    case 0: c = v >> 7; return ((v << 1) & 0xFF) | c;
+    case 1: c = v & 1; return (v >> 1) | (c << 7);
+    case 2: c = v >> 7; return ((v << 1) & 0xFF) | oc;
+    case 3: c = v & 1; return (v >> 1) | (oc << 7);
+    case 4: c = v >> 7; return (v << 1) & 0xFF;
+    case 5: c = v & 1; return (v >> 1) | (v & 0x80);
+    case 6: c = 0; return ((v & 0xF) << 4) | (v >> 4);
+    default: c = v & 1; return v >> 1;
+  }
+}
+
 struct Hot {
   uint32_t bcde, hlxa;  // B C D E | H L - A, high byte first
   int f, pc, sp;
@@ -903,8 +920,7 @@ struct Emu {
   // ends, banks outside the window)
   __device__ __noinline__ uint32_t fetch_slow(int at, const uint8_t* dec) {
     const int op = read8(at), b1 = read8((at + 1) & 0xFFFF), b2 = read8((at + 2) & 0xFFFF);
-    uint32_t e = dec[op];
-    if (op == 0xCB && (b1 & 7) == 6) e |= RD_HL << 5;
+    const uint32_t e = op == 0xCB ? cb_family(b1) : dec[op];
     return (uint32_t)op | ((uint32_t)b1 << 8) | ((uint32_t)b2 << 16) | (e << 24);
   }
   // the exact tail of one instruction plus the halted iterations it leads
@@ -1105,7 +1121,7 @@ __global__ void __launch_bounds__(MAXT, 1)
     const int opcode = w & 0xFF;
     const int imm8 = (w >> 8) & 0xFF;
     const int imm16 = (w >> 8) & 0xFFFF;
-    const int fam = (w >> 24) & 31;
+    const int fam = w >> 24;
     if (DBG) {  // checks before execution (:1320-1338)
       if (dbg.trap_pc && pc == dbg.trap_pc) { s.trap_op(pc, opcode, 5); break; }
       if (dbg.trap_rst38 && opcode == 0xFF && pc != 0x0038) { s.trap_op(pc, opcode, 3); break; }
@@ -1211,7 +1227,25 @@ __global__ void __launch_bounds__(MAXT, 1)
       case FM_LDR_HL: h.setr(y, rd(h.HL())); cyc = 8; break;
       case FM_STHL_R: nw = 1; wa0 = h.HL(); wv0 = h.getr(z); cyc = 8; break;
       case FM_HALT: s.halted = 1; s.ev |= EV_HALT; h.next_ev = INT_MIN; break;
-      case FM_ALU_R: h.alu(y, h.getr(z)); break;
+      case FM_ALU_ADC: {  // ADD, ADC (alu.py)
+        const int a = h.A(), v = h.getr(z), cin = y & (h.f >> 4) & 1, r = a + v + cin;
+        h.f = (((r & 0xFF) == 0) << 7) | ((((a & 0xF) + (v & 0xF) + cin) > 0xF) << 5) | ((r > 0xFF) << 4);
+        h.setA(r);
+        break;
+      }
+      case FM_ALU_SBC: {  // SUB, SBC, CP
+        const int a = h.A(), v = h.getr(z), cin = y == 3 ? (h.f >> 4) & 1 : 0, r = a - v - cin;
+        h.f = (((r & 0xFF) == 0) << 7) | 0x40 | ((((a & 0xF) - (v & 0xF) - cin) < 0) << 5) | ((r < 0) << 4);
+        if (y != 7) h.setA(r);
+        break;
+      }
+      case FM_ALU_LOG: {  // AND, XOR, OR
+        const int a = h.A(), v = h.getr(z);
+        const int r = y == 4 ? (a & v) : y == 5 ? (a ^ v) : (a | v);
+        h.f = ((r == 0) << 7) | (y == 4 ? 0x20 : 0);
+        h.setA(r);
+        break;
+      }
       case FM_ALU_V: {
         const bool hl = opcode < 0xC0;  // ALU A,(HL); else ALU A,d8
         h.alu(y, hl ? rd(h.HL()) : imm8);
@@ -1267,37 +1301,45 @@ __global__ void __launch_bounds__(MAXT, 1)
         h.sp = (h.sp - 2) & 0xFFFF;
         npc = opcode & 0x38; cyc = 16; break;
       }
-      case FM_CB: {
-        // bitops.py: RLC RRC RL RR SLA SRA SWAP SRL, BIT, RES, SET
-        const int cb = imm8, cz = cb & 7, cy = (cb >> 3) & 7, grp = cb >> 6;
-        const bool hl = cz == 6;
-        const int v = hl ? rd(h.HL()) : h.getr(cz);
+      // CB-prefixed (bitops.py): RLC RRC RL RR SLA SRA SWAP SRL, BIT, RES, SET
+      case FM_CB_ROT: {
+        const int cz = imm8 & 7;
+        int c;
+        const int res = cb_rot((imm8 >> 3) & 7, h.getr(cz), (h.f >> 4) & 1, c);
+        h.f = ((res == 0) << 7) | (c << 4);
+        h.setr(cz, res);
+        npc = pc + 2; cyc = 8; break;
+      }
+      case FM_CB_BIT:  // Z from the bit, H set, C kept
+        h.f = ((((h.getr(imm8 & 7) >> ((imm8 >> 3) & 7)) & 1) ^ 1) << 7) | 0x20 | (h.f & 0x10);
+        npc = pc + 2; cyc = 8; break;
+      case FM_CB_RES: {
+        const int cz = imm8 & 7;
+        h.setr(cz, h.getr(cz) & ~(1 << ((imm8 >> 3) & 7)));
+        npc = pc + 2; cyc = 8; break;
+      }
+      case FM_CB_SET: {
+        const int cz = imm8 & 7;
+        h.setr(cz, h.getr(cz) | (1 << ((imm8 >> 3) & 7)));
+        npc = pc + 2; cyc = 8; break;
+      }
+      case FM_CB_HL: {  // the (HL) forms
+        const int cy = (imm8 >> 3) & 7, grp = imm8 >> 6, v = rd(h.HL());
         npc = pc + 2;
-        if (grp == 1) {  // BIT: Z from the bit, H set, C kept
+        if (grp == 1) {
           h.f = ((((v >> cy) & 1) ^ 1) << 7) | 0x20 | (h.f & 0x10);
-          cyc = hl ? 12 : 8;
+          cyc = 12;
           break;
         }
         int res;
         if (grp == 0) {
-          const int oc = (h.f >> 4) & 1;
           int c;
-          switch (cy) {
-            case 0: c = v >> 7; res = ((v << 1) & 0xFF) | c; break;
-            case 1: c = v & 1; res = (v >> 1) | (c << 7); break;
-            case 2: c = v >> 7; res = ((v << 1) & 0xFF) | oc; break;
-            case 3: c = v & 1; res = (v >> 1) | (oc << 7); break;
-            case 4: c = v >> 7; res = (v << 1) & 0xFF; break;
-            case 5: c = v & 1; res = (v >> 1) | (v & 0x80); break;
-            case 6: c = 0; res = ((v & 0xF) << 4) | (v >> 4); break;
-            default: c = v & 1; res = v >> 1; break;
-          }
+          res = cb_rot(cy, v, (h.f >> 4) & 1, c);
           h.f = ((res == 0) << 7) | (c << 4);
         } else {
           res = grp == 2 ? (v & ~(1 << cy) & 0xFF) : (v | (1 << cy));
         }
-        if (hl) { nw = 1; wa0 = h.HL(); wv0 = res; cyc = 16; }
-        else { h.setr(cz, res); cyc = 8; }
+        nw = 1; wa0 = h.HL(); wv0 = res; cyc = 16;
         break;
       }
       case FM_SPADD:
