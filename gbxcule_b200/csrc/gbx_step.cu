@@ -646,15 +646,17 @@ struct Emu {
     return v | 0xC0;
   }
 
+  // JOYP select write: the register latches the selected group's buttons
+  __device__ __forceinline__ void write_joyp(int val) {
+    const int sel = val & 0x30;
+    u8s[(size_t)F_JOYP_SELECT * S] = (uint8_t)sel;
+    joyp = joyp_value(sel);
+  }
+
   __device__ void write_io(int a, int val) {
     const int v8 = val & 0xFF;
     switch (a & 0xFF) {
-      case 0x00: {
-        int sel = v8 & 0x30;
-        u8s[(size_t)F_JOYP_SELECT * S] = (uint8_t)sel;
-        joyp = joyp_value(sel);
-        return;
-      }
+      case 0x00: write_joyp(v8); return;
       case 0x0F: iflag = v8 & 0x1F; ev |= EV_IRQ; return;
       case 0x02:
         if ((val & 0x80) && (val & 0x01)) {
@@ -1092,12 +1094,14 @@ __global__ void __launch_bounds__(MAXT, 1)
   auto rd = [&](int a) -> int {
     if (plain(a)) return mem[a];
     if ((unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0) return cram[cram_off + a - 0xA000];
+    if (a == 0xFF00) return s.joyp;  // JOYP: no clock, no side effect
     s.clk = h.clk;  // lazy DIV/TIMA/STAT/LY reads need the clock
     return s.read_slow(a);
   };
   auto wr = [&](int a, int v) {
     if (plain(a)) { mem[a] = (uint8_t)v; return; }
     if ((unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0) { cram[cram_off + a - 0xA000] = (uint8_t)v; return; }
+    if (a == 0xFF00) { s.write_joyp(v); return; }  // JOYP select: no event, no sync
     s.clk = h.clk;
     s.write_slow(a, v);  // ev is 0 here unless an earlier write of this instruction set it
     h.clk = s.clk;       // a timing write syncs (clk = 0) and sets ev
