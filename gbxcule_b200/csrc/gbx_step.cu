@@ -1260,7 +1260,12 @@ __global__ void __launch_bounds__(MAXT, 1)
         if (opcode == 0xC9 || opcode == 0xD9 || h.cond(y)) {
           npc = rd(h.sp) | (rd((h.sp + 1) & 0xFFFF) << 8);
           h.sp = (h.sp + 2) & 0xFFFF;
-          if (opcode == 0xD9) { s.ime = 1; s.ime_delay = 0; s.ev |= EV_IRQ; h.next_ev = INT_MIN; }
+          if (opcode == 0xD9) {
+            s.ime_delay = 0;
+            // Setting IME can make a pending interrupt serviceable; with IME
+            // already set none is pending (every IF/IE change is an event).
+            if (!s.ime) { s.ime = 1; s.ev |= EV_IRQ; h.next_ev = INT_MIN; }
+          }
           cyc = (opcode & 1) ? 16 : 20;
         } else {
           cyc = 8;
@@ -1356,10 +1361,13 @@ __global__ void __launch_bounds__(MAXT, 1)
           npc = pc + 2;
         }
         break;
-      case FM_IME:
+      case FM_IME:  // EI, DI (misc.py); EI with IME already set changes nothing (see RETI)
         s.ime_delay = 0;
-        if (opcode == 0xFB) { s.ime = 1; s.ev |= EV_IRQ; h.next_ev = INT_MIN; }
-        else s.ime = 0;
+        if (opcode == 0xFB) {
+          if (!s.ime) { s.ime = 1; s.ev |= EV_IRQ; h.next_ev = INT_MIN; }
+        } else {
+          s.ime = 0;
+        }
         break;
       default:  // FM_TRAP (misc.py:42-56)
         s.trap_op(pc, opcode, 1);
