@@ -146,6 +146,18 @@ def _issue_roofline(emu_instr_per_s_per_gpu: float, clk: dict) -> dict:
             "note": "warp instructions per emulated instruction from an ncu capture of this workload"}
 
 
+def _cpu_model() -> str:
+    """Host CPU model name (Linux /proc/cpuinfo), recorded beside the CPU baseline."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_oracle_rate(total_envs_hint: int, warmup: int, steps: int, threads: int, seed: int = 0) -> dict:
     """Time the CPU oracle on a bounded sample of the workload (env-steps/s)."""
     from gbxcule_b200 import roms
@@ -162,7 +174,7 @@ def cpu_oracle_rate(total_envs_hint: int, warmup: int, steps: int, threads: int,
         o.step(roms.uniform_actions(rng, m, 9), FRAMES, RELEASE)
         o.render_packed()
     dt = time.perf_counter() - t0
-    return {"value": m * steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
+    return {"value": m * steps / dt, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": _cpu_model(),
             "sample": f"{m} envs x {steps} env-steps (after {warmup} warm-up steps) of the config-2 workload, "
                       f"oracle step + packed render, {threads} threads, {dt:.1f} s"}
 
