@@ -343,6 +343,7 @@ def run_rollout_workload(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
+    torch.backends.cudnn.benchmark = True  # the policy's conv shapes repeat every step
     n = args.envs or 131072
     K, W = args.steps, args.warmup
     be = GbxVecCudaBackend(roms.config5_rom(), num_envs=n, frames_per_step=FRAMES,

@@ -33,13 +33,24 @@ def unpack_lut(device) -> Any:
     return _LUT[key]
 
 
+_SHIFTS: dict[str, Any] = {}
+
+
 def unpack_2bpp_u8(packed) -> Any:
-    """Unpack uint8 2 bpp bytes along the last axis (rl/packed_pixels.py:62-71)."""
+    """Unpack uint8 2 bpp bytes along the last axis (rl/packed_pixels.py:62-71).
+
+    Same result as the 256 x 4 lookup table (first pixel in bits 0-1),
+    computed as one broadcast shift-and-mask on uint8, without an int64
+    index tensor.
+    """
     import torch
 
     if packed.dtype is not torch.uint8:
         raise ValueError("packed_u8 must be uint8")
-    out = unpack_lut(packed.device)[packed.to(torch.int64)]
+    key = str(packed.device)
+    if key not in _SHIFTS:
+        _SHIFTS[key] = torch.tensor([0, 2, 4, 6], dtype=torch.uint8, device=packed.device)
+    out = torch.bitwise_right_shift(packed.unsqueeze(-1), _SHIFTS[key]).bitwise_and_(3)
     return out.reshape(*packed.shape[:-1], packed.shape[-1] * 4)
 
 
@@ -71,8 +82,10 @@ def _policy_class():
             self.head = nn.Sequential(nn.Linear(flat, 512), nn.ReLU(), nn.Linear(512, num_actions))
 
         def forward(self, frames_u8):  # [B, 72, 80] uint8 shades
+            # one channel: NCHW and NHWC are the same bytes; channels-last
+            # keeps every conv in NHWC (no layout transposes around cuDNN)
             x = frames_u8.unsqueeze(1).to(self.head[0].weight.dtype) / 3.0
-            return self.head(self.conv(x))
+            return self.head(self.conv(x.contiguous(memory_format=torch.channels_last)))
 
     return PixelPolicy
 
@@ -83,7 +96,7 @@ def make_policy(device, *, num_actions: int = 9, seed: int = 0, dtype=None):
 
     torch.manual_seed(seed)
     pol = _policy_class()(num_actions).to(device=device, dtype=dtype or torch.bfloat16)
-    return pol.eval()
+    return pol.to(memory_format=torch.channels_last).eval()
 
 
 @dataclass
