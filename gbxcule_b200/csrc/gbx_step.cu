@@ -1529,9 +1529,6 @@ static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int
   if (dbg.active())  // debug traps: one instantiation (its 64-register bound fits every block size)
     return launch_t<MBC, 1024, true>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
                                      rom_words, sm, dbg);
-  if (K > 1 && threads > 768 && threads <= 896)  // 28 warps of 32 envs: 72 registers instead of 64
-    return launch_t<MBC, 896, false>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
-                                     rom_words, sm, dbg);
   if (threads <= 256)
     return launch_t<MBC, 256, false>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
                                      rom_words, sm, dbg);
