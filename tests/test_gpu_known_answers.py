@@ -189,3 +189,66 @@ def test_serial_readback_matches_oracle(micro_roms):
         assert int(be.export_state(0, 1)["serial_len"][0]) == 0
     finally:
         be.close()
+
+
+def _ime_rom() -> bytes:
+    """Every IME transition in a loop: EI and RETI with an interrupt pending
+    and with none, EI with IME already set, IF writes with IME on and off."""
+    from gbxcule_b200.roms import Asm, finalize_header
+
+    a = Asm(0x8000)
+    for v in range(0, 0x40, 8):
+        a.org(v)
+        a.db(0xC9)                        # RST vectors: RET
+    a.org(0x40)
+    a.db(0x04, 0xD9)                      # VBlank vector: INC B; RETI
+    a.org(0x48)
+    a.db(0x14, 0xD9)                      # STAT vector: INC D; RETI
+    a.org(0x150)
+    a.ld_rr("sp", 0xDFF0)
+    a.ld_r_d8("a", 0x00)
+    a.ldh_store(0x40)                     # LCD off: IF changes only by writes
+    a.ld_r_d8("a", 0x03)
+    a.ldh_store(0xFF)                     # IE = VBlank | STAT
+    a.label("loop")
+    a.ld_r_d8("a", 0x01)
+    a.ldh_store(0x0F)                     # IF = VBlank, IME = 0: pending, not serviced
+    a.db(0x00)                            # NOP
+    a.db(0xFB)                            # EI: IME 0 -> 1 with VBlank pending
+    a.db(0x00)
+    a.db(0xFB)                            # EI with IME already set, nothing pending
+    a.ld_r_d8("a", 0x02)
+    a.ldh_store(0x0F)                     # IF = STAT with IME set: serviced next
+    a.db(0x0C)                            # INC C
+    a.db(0xF3)                            # DI
+    a.ld_r_d8("a", 0x03)
+    a.ldh_store(0x0F)                     # both pending, IME = 0
+    a.call("sub")                         # RETI there: IME 0 -> 1 with both pending
+    a.db(0x1C)                            # INC E
+    a.db(0xF3)                            # DI
+    a.call("sub")                         # RETI with nothing pending
+    a.db(0xFB)                            # EI, nothing pending
+    a.jp("loop")
+    a.label("sub")
+    a.db(0xD9)
+    return finalize_header(bytearray(a.finish()), title="IMEMIX", cart_type=0, rom_code=0, ram_code=0)
+
+
+def test_ime_transitions_match_oracle():
+    """The exact tail after EI/RETI (taken only when IME goes 0 -> 1) and
+    after IF/IE writes services interrupts exactly where the reference does."""
+    rom = _ime_rom()
+    n = 3
+    be = _backend(rom, n, frames=3)
+    o = OracleEnvs(rom, roms.boot_stub(), n)
+    try:
+        rng = np.random.default_rng(9)
+        for _ in range(3):
+            acts = roms.uniform_actions(rng, n, 9)
+            be.step_torch(torch.as_tensor(acts, device="cuda"))
+            o.step(acts, 3, 1)
+            got = be.export_state()
+            assert not st.diff(got, o.state(), n)
+        assert int(got["b"][0]) > 0 and int(got["d"][0]) > 0  # both handlers ran
+    finally:
+        be.close()
