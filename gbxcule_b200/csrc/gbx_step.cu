@@ -1123,9 +1123,14 @@ __global__ void __launch_bounds__(MAXT, 1)
       w = s.fetch_slow(pc, dec_s);
     }
     const int opcode = w & 0xFF;
-    const int imm8 = (w >> 8) & 0xFF;
-    const int imm16 = (w >> 8) & 0xFFFF;
     const int fam = w >> 24;
+    // Operand fields are extracted inside the cases that use them: hoisted
+    // above the switch they cost every instruction (NOP 55 -> 49 warp
+    // instructions without them).
+#define IMM8 ((int)((w >> 8) & 0xFF))
+#define IMM16 ((int)((w >> 8) & 0xFFFF))
+#define YF ((opcode >> 3) & 7)
+#define ZF (opcode & 7)
     if (DBG) {  // checks before execution (:1320-1338)
       if (dbg.trap_pc && pc == dbg.trap_pc) { s.trap_op(pc, opcode, 5); break; }
       if (dbg.trap_rst38 && opcode == 0xFF && pc != 0x0038) { s.trap_op(pc, opcode, 3); break; }
@@ -1135,11 +1140,10 @@ __global__ void __launch_bounds__(MAXT, 1)
     // ---- execute ----
     int npc = pc + 1;
     int cyc = 4;
-    int nw = 0, wa0 = 0, wv0 = 0, wa1 = 0, wv1 = 0;
-    const int y = (opcode >> 3) & 7, z = opcode & 7;
+    int nw = 0, wa0, wv0, wa1, wv1;  // the slots are read only below nw
     switch (fam) {
-      case FM_LDRR: h.setr(y, h.getr(z)); break;  // includes NOP (LD B,B form)
-      case FM_LD16: h.setp((opcode >> 4) & 3, imm16); npc = pc + 3; cyc = 12; break;
+      case FM_LDRR: h.setr(YF, h.getr(ZF)); break;  // includes NOP (LD B,B form)
+      case FM_LD16: h.setp((opcode >> 4) & 3, IMM16); npc = pc + 3; cyc = 12; break;
       case FM_ST_A:
         nw = 1; wv0 = h.A();
         if (opcode < 0x40) {
@@ -1148,9 +1152,9 @@ __global__ void __launch_bounds__(MAXT, 1)
           wa0 = ad;
           if (p >= 2) h.setHL(p == 2 ? ad + 1 : ad - 1);
           cyc = 8;
-        } else if (opcode == 0xE0) { wa0 = 0xFF00 | imm8; npc = pc + 2; cyc = 12; }
+        } else if (opcode == 0xE0) { wa0 = 0xFF00 | IMM8; npc = pc + 2; cyc = 12; }
         else if (opcode == 0xE2) { wa0 = 0xFF00 | h.C_(); cyc = 8; }
-        else { wa0 = imm16; npc = pc + 3; cyc = 16; }
+        else { wa0 = IMM16; npc = pc + 3; cyc = 16; }
         break;
       case FM_LD_A:
         if (opcode < 0x40) {
@@ -1159,9 +1163,9 @@ __global__ void __launch_bounds__(MAXT, 1)
           h.setA(rd(ad));
           if (p >= 2) h.setHL(p == 2 ? ad + 1 : ad - 1);
           cyc = 8;
-        } else if (opcode == 0xF0) { h.setA(rd(0xFF00 | imm8)); npc = pc + 2; cyc = 12; }
+        } else if (opcode == 0xF0) { h.setA(rd(0xFF00 | IMM8)); npc = pc + 2; cyc = 12; }
         else if (opcode == 0xF2) { h.setA(rd(0xFF00 | h.C_())); cyc = 8; }
-        else { h.setA(rd(imm16)); npc = pc + 3; cyc = 16; }
+        else { h.setA(rd(IMM16)); npc = pc + 3; cyc = 16; }
         break;
       case FM_INCDEC16: {
         const int p = (opcode >> 4) & 3;
@@ -1169,24 +1173,24 @@ __global__ void __launch_bounds__(MAXT, 1)
         cyc = 8; break;
       }
       case FM_INCDEC8: {
-        const int dec1 = z & 1;
-        const int old = h.getr(y), v = (dec1 ? old - 1 : old + 1) & 0xFF;
-        h.setr(y, v);
+        const int dec1 = ZF & 1;
+        const int old = h.getr(YF), v = (dec1 ? old - 1 : old + 1) & 0xFF;
+        h.setr(YF, v);
         h.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (h.f >> 4) & 1);
         break;
       }
       case FM_INCDEC_HL: {
-        const int old = rd(h.HL()), dec1 = z & 1;
+        const int old = rd(h.HL()), dec1 = ZF & 1;
         const int v = (dec1 ? old - 1 : old + 1) & 0xFF;
         h.f = FLAGS(v == 0, dec1, dec1 ? (old & 0xF) == 0 : (old & 0xF) == 0xF, (h.f >> 4) & 1);
         nw = 1; wa0 = h.HL(); wv0 = v;
         cyc = 12; break;
       }
-      case FM_LD8_IMM: h.setr(y, imm8); npc = pc + 2; cyc = 8; break;
-      case FM_ST_HL_IMM: nw = 1; wa0 = h.HL(); wv0 = imm8; npc = pc + 2; cyc = 12; break;
+      case FM_LD8_IMM: h.setr(YF, IMM8); npc = pc + 2; cyc = 8; break;
+      case FM_ST_HL_IMM: nw = 1; wa0 = h.HL(); wv0 = IMM8; npc = pc + 2; cyc = 12; break;
       case FM_ROTA: {
         const int a = h.A(), oc = (h.f >> 4) & 1;
-        const int right = y & 1, thru = y >> 1;
+        const int right = YF & 1, thru = YF >> 1;
         const int c = right ? (a & 1) : ((a >> 7) & 1);
         const int in = thru ? oc : c;
         const int r = right ? ((a >> 1) | (in << 7)) : (((a << 1) & 0xFF) | in);
@@ -1194,7 +1198,7 @@ __global__ void __launch_bounds__(MAXT, 1)
         break;
       }
       case FM_ST_SP16:
-        nw = 2; wa0 = imm16; wv0 = h.sp & 0xFF; wa1 = (imm16 + 1) & 0xFFFF; wv1 = (h.sp >> 8) & 0xFF;
+        nw = 2; wa0 = IMM16; wv0 = h.sp & 0xFF; wa1 = (IMM16 + 1) & 0xFFFF; wv1 = (h.sp >> 8) & 0xFF;
         npc = pc + 3; cyc = 20; break;
       case FM_ADDHL: {
         const int hl = h.HL(), rr = h.getp((opcode >> 4) & 3), sum = hl + rr;
@@ -1203,8 +1207,8 @@ __global__ void __launch_bounds__(MAXT, 1)
         cyc = 8; break;
       }
       case FM_JR: {
-        const bool t = opcode == 0x18 || h.cond(y);
-        npc = pc + 2 + (t ? sign8(imm8) : 0);
+        const bool t = opcode == 0x18 || h.cond(YF);
+        npc = pc + 2 + (t ? sign8(IMM8) : 0);
         cyc = t ? 12 : 8;
         break;
       }
@@ -1222,42 +1226,42 @@ __global__ void __launch_bounds__(MAXT, 1)
         h.f = FLAGS(a == 0, n, 0, carry); h.setA(a);
         break;
       }
-      case FM_FLAGOP: {  // CPL (y=5), SCF (y=6), CCF (y=7)
+      case FM_FLAGOP: {  // CPL (YF=5), SCF (YF=6), CCF (YF=7)
         const int zf = (h.f >> 7) & 1, cf = (h.f >> 4) & 1;
-        if (y == 5) { h.setA(h.A() ^ 0xFF); h.f = FLAGS(zf, 1, 1, cf); }
-        else h.f = FLAGS(zf, 0, 0, y == 6 ? 1 : !cf);
+        if (YF == 5) { h.setA(h.A() ^ 0xFF); h.f = FLAGS(zf, 1, 1, cf); }
+        else h.f = FLAGS(zf, 0, 0, YF == 6 ? 1 : !cf);
         break;
       }
-      case FM_LDR_HL: h.setr(y, rd(h.HL())); cyc = 8; break;
-      case FM_STHL_R: nw = 1; wa0 = h.HL(); wv0 = h.getr(z); cyc = 8; break;
+      case FM_LDR_HL: h.setr(YF, rd(h.HL())); cyc = 8; break;
+      case FM_STHL_R: nw = 1; wa0 = h.HL(); wv0 = h.getr(ZF); cyc = 8; break;
       case FM_HALT: s.halted = 1; s.ev |= EV_HALT; h.next_ev = INT_MIN; break;
       case FM_ALU_ADC: {  // ADD, ADC (alu.py)
-        const int a = h.A(), v = h.getr(z), cin = y & (h.f >> 4) & 1, r = a + v + cin;
+        const int a = h.A(), v = h.getr(ZF), cin = YF & (h.f >> 4) & 1, r = a + v + cin;
         h.f = (((r & 0xFF) == 0) << 7) | ((((a & 0xF) + (v & 0xF) + cin) > 0xF) << 5) | ((r > 0xFF) << 4);
         h.setA(r);
         break;
       }
       case FM_ALU_SBC: {  // SUB, SBC, CP
-        const int a = h.A(), v = h.getr(z), cin = y == 3 ? (h.f >> 4) & 1 : 0, r = a - v - cin;
+        const int a = h.A(), v = h.getr(ZF), cin = YF == 3 ? (h.f >> 4) & 1 : 0, r = a - v - cin;
         h.f = (((r & 0xFF) == 0) << 7) | 0x40 | ((((a & 0xF) - (v & 0xF) - cin) < 0) << 5) | ((r < 0) << 4);
-        if (y != 7) h.setA(r);
+        if (YF != 7) h.setA(r);
         break;
       }
       case FM_ALU_LOG: {  // AND, XOR, OR
-        const int a = h.A(), v = h.getr(z);
-        const int r = y == 4 ? (a & v) : y == 5 ? (a ^ v) : (a | v);
-        h.f = ((r == 0) << 7) | (y == 4 ? 0x20 : 0);
+        const int a = h.A(), v = h.getr(ZF);
+        const int r = YF == 4 ? (a & v) : YF == 5 ? (a ^ v) : (a | v);
+        h.f = ((r == 0) << 7) | (YF == 4 ? 0x20 : 0);
         h.setA(r);
         break;
       }
       case FM_ALU_V: {
         const bool hl = opcode < 0xC0;  // ALU A,(HL); else ALU A,d8
-        h.alu(y, hl ? rd(h.HL()) : imm8);
+        h.alu(YF, hl ? rd(h.HL()) : IMM8);
         npc = pc + (hl ? 1 : 2);
         cyc = 8; break;
       }
       case FM_RET:
-        if (opcode == 0xC9 || opcode == 0xD9 || h.cond(y)) {
+        if (opcode == 0xC9 || opcode == 0xD9 || h.cond(YF)) {
           npc = rd(h.sp) | (rd((h.sp + 1) & 0xFFFF) << 8);
           h.sp = (h.sp + 2) & 0xFFFF;
           if (opcode == 0xD9) {
@@ -1282,17 +1286,17 @@ __global__ void __launch_bounds__(MAXT, 1)
       case FM_JP:
         if (opcode == 0xE9) { npc = h.HL(); break; }
         {
-          const bool t = opcode == 0xC3 || h.cond(y);
-          npc = t ? imm16 : pc + 3;
+          const bool t = opcode == 0xC3 || h.cond(YF);
+          npc = t ? IMM16 : pc + 3;
           cyc = t ? 16 : 12;
         }
         break;
       case FM_CALL:
-        if (opcode == 0xCD || h.cond(y)) {
+        if (opcode == 0xCD || h.cond(YF)) {
           const int ret = (pc + 3) & 0xFFFF;
           nw = 2; wa0 = (h.sp - 1) & 0xFFFF; wv0 = ret >> 8; wa1 = (h.sp - 2) & 0xFFFF; wv1 = ret & 0xFF;
           h.sp = (h.sp - 2) & 0xFFFF;
-          npc = imm16; cyc = 24;
+          npc = IMM16; cyc = 24;
         } else {
           npc = pc + 3; cyc = 12;
         }
@@ -1312,28 +1316,28 @@ __global__ void __launch_bounds__(MAXT, 1)
       }
       // CB-prefixed (bitops.py): RLC RRC RL RR SLA SRA SWAP SRL, BIT, RES, SET
       case FM_CB_ROT: {
-        const int cz = imm8 & 7;
+        const int cz = IMM8 & 7;
         int c;
-        const int res = cb_rot((imm8 >> 3) & 7, h.getr(cz), (h.f >> 4) & 1, c);
+        const int res = cb_rot((IMM8 >> 3) & 7, h.getr(cz), (h.f >> 4) & 1, c);
         h.f = ((res == 0) << 7) | (c << 4);
         h.setr(cz, res);
         npc = pc + 2; cyc = 8; break;
       }
       case FM_CB_BIT:  // Z from the bit, H set, C kept
-        h.f = ((((h.getr(imm8 & 7) >> ((imm8 >> 3) & 7)) & 1) ^ 1) << 7) | 0x20 | (h.f & 0x10);
+        h.f = ((((h.getr(IMM8 & 7) >> ((IMM8 >> 3) & 7)) & 1) ^ 1) << 7) | 0x20 | (h.f & 0x10);
         npc = pc + 2; cyc = 8; break;
       case FM_CB_RES: {
-        const int cz = imm8 & 7;
-        h.setr(cz, h.getr(cz) & ~(1 << ((imm8 >> 3) & 7)));
+        const int cz = IMM8 & 7;
+        h.setr(cz, h.getr(cz) & ~(1 << ((IMM8 >> 3) & 7)));
         npc = pc + 2; cyc = 8; break;
       }
       case FM_CB_SET: {
-        const int cz = imm8 & 7;
-        h.setr(cz, h.getr(cz) | (1 << ((imm8 >> 3) & 7)));
+        const int cz = IMM8 & 7;
+        h.setr(cz, h.getr(cz) | (1 << ((IMM8 >> 3) & 7)));
         npc = pc + 2; cyc = 8; break;
       }
       case FM_CB_HL: {  // the (HL) forms
-        const int cy = (imm8 >> 3) & 7, grp = imm8 >> 6, v = rd(h.HL());
+        const int cy = (IMM8 >> 3) & 7, grp = IMM8 >> 6, v = rd(h.HL());
         npc = pc + 2;
         if (grp == 1) {
           h.f = ((((v >> cy) & 1) ^ 1) << 7) | 0x20 | (h.f & 0x10);
@@ -1354,7 +1358,7 @@ __global__ void __launch_bounds__(MAXT, 1)
       case FM_SPADD:
         if (opcode == 0xF9) { h.sp = h.HL(); cyc = 8; break; }
         {
-          const int ou = imm8, res = (h.sp + sign8(imm8)) & 0xFFFF;
+          const int ou = IMM8, res = (h.sp + sign8(IMM8)) & 0xFFFF;
           h.f = FLAGS(0, 0, ((h.sp & 0xF) + (ou & 0xF)) > 0xF, ((h.sp & 0xFF) + ou) > 0xFF);
           if (opcode == 0xE8) { h.sp = res; cyc = 16; }
           else { h.setHL(res); cyc = 12; }
@@ -1376,6 +1380,10 @@ __global__ void __launch_bounds__(MAXT, 1)
         cyc = 0;
         break;
     }
+#undef IMM8
+#undef IMM16
+#undef YF
+#undef ZF
     h.pc = npc & 0xFFFF;
     // ---- memory writes ----
     if (nw) {
