@@ -169,10 +169,13 @@ struct Hot {
   __device__ __forceinline__ int BC() const { return bcde >> 16; }
   __device__ __forceinline__ int DE() const { return bcde & 0xFFFF; }
   __device__ __forceinline__ int C_() const { return (bcde >> 16) & 0xFF; }
-  // r8 index: 0 B, 1 C, 2 D, 3 E, 4 H, 5 L, 7 A (6 = (HL), never passed).
-  // {bcde, hlxa} read as one 8-byte array puts register i at byte i ^ 3.
+  // r8 index 0..7: 0 B, 1 C, 2 D, 3 E, 4 H, 5 L, 7 A (6 = (HL), never passed;
+  // the decode sends every (HL) form to its own family). {bcde, hlxa} read
+  // as one 8-byte array puts register i at byte i ^ 3; byte 5 (hlxa's unused
+  // byte) is always 0, so selecting it for the upper three result bytes
+  // returns the register zero-extended without a mask.
   __device__ __forceinline__ int getr(int i) const {
-    return __byte_perm(bcde, hlxa, (i ^ 3) & 7) & 0xFF;
+    return __byte_perm(bcde, hlxa, (i ^ 3) | 0x5550);
   }
   __device__ __forceinline__ static uint32_t insert_byte(uint32_t w, int v, int pos) {
     uint32_t r;
