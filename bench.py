@@ -61,11 +61,11 @@ STEP_STATE_BYTES = 2 * (27 * 4 + 2 * 8 + 3 + 20 * 4 + 12) + 4 + 32 * 4
 # `bench.py --steps 3 --warmup 3 --no-cpu-baseline`. It includes the
 # emulated programs' RAM lines and the write-back of the L2 flush buffer
 # written just before the launch.
-STEP_KERNEL_DRAM_BYTES_4096 = 64.549888e6 + 145.515264e6
+STEP_KERNEL_DRAM_BYTES_4096 = 64.935168e6 + 146.290944e6
 # smsp__inst_executed.sum / emulated SM83 instructions of one step-kernel
 # launch on this workload, from the same ncu capture: the integer-issue cost
 # of one emulated instruction, used for the issue roofline below.
-WARP_INSTR_PER_EMULATED_INSTR = 52.546751982e9 / (4096 * 197327.3)
+WARP_INSTR_PER_EMULATED_INSTR = 48.096002450e9 / (4096 * 197327.3)
 SMS, ISSUE_PER_SM_PER_CLOCK = 148, 4
 
 
