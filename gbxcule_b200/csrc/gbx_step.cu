@@ -15,25 +15,29 @@
 //    LYC, WY, IE) live in registers; every path that touches those addresses
 //    (CPU access, OAM DMA source, env-0 latches) goes through the cache.
 //  * Fetch: the ROM is pre-decoded on the host into one 32-bit word per byte
-//    (opcode, 16-bit immediate, family, memory-read mode). Banks 0-1 of it sit
-//    in shared memory, so fetch + decode is a single 4-byte shared load; other
-//    banks come through the read-only path. Code outside ROM (RAM, the boot
-//    ROM overlay, bank-crossing fetches) is decoded from bytes.
-//  * Execute: one read site, one switch over 30 families of SM83's regular
-//    encoding (registers packed into two u32, indexed by bit-field extract;
-//    ALU and CB families branch-free), one write site.
+//    (opcode, 16-bit immediate, family). Banks 0-1 of it sit in shared
+//    memory, so fetch + decode is a single 4-byte shared load; other banks
+//    come through the read-only path. Code outside ROM (RAM, the boot ROM
+//    overlay, bank-crossing fetches) is decoded from bytes.
+//  * Execute: one switch over 36 families of SM83's regular encoding (the
+//    CB and ALU register forms split by operation). Registers are packed
+//    into two u32, read with one byte-permute and written with one bit-field
+//    insert; operand fields are extracted inside the cases that use them;
+//    memory operands are read inside their families (plain RAM, the mapped
+//    cart-RAM bank and JOYP inline, the rest out of line); one write site.
 //  * Post-instruction work is lazy. The reference updates timer, DIV, STAT
 //    mode bits, stat_prev, LY, RTC and the frame counter after every
 //    instruction. Here one counter `clk` accumulates cycles and is compared
 //    with `next_ev`, the cycles until the earliest event (timer edge/reload,
 //    scanline boundary, frame end, RTC second). Until then every one of those
 //    values is a function of the state at the last sync plus `clk`, so the
-//    common instruction tail is `clk += cyc; if (clk >= next_ev | ev) ...`.
-//    An instruction that crosses an event, halts, traps, or writes a port
-//    with timing side effects (LCDC, LY, LYC, IF, IE, timer, RTC) or enables
-//    interrupts sets `ev` and runs the reference's post-processing verbatim on
-//    materialised state (slow_post). The reference's timer_tick is additive
-//    over time, so lumping event-free cycles is exact.
+//    common instruction tail is `clk += cyc; if (clk >= next_ev) ...`. An
+//    instruction that crosses an event, halts, traps, writes a port with
+//    timing side effects (LCDC, STAT, LY, LYC, WY, IF, IE, timer, RTC) or
+//    sets IME from 0 forces `next_ev` and runs the reference's
+//    post-processing verbatim on materialised state (slow_post). The
+//    reference's timer_tick is additive over time, so lumping event-free
+//    cycles is exact.
 //  * HALT: runs of 4-cycle halted iterations that cannot change anything
 //    observable except counters (no line boundary, no timer reload, no frame
 //    end) are applied in one batch.
