@@ -265,7 +265,7 @@ struct Emu {
   // cart
   int ram_en, bank_lo, bank_hi, ram_bank, bank_mode, bootrom, rtc_sel, rtc_latch;
   int bank0_off, bankN_off;   // ROM byte offset of a bank region; -1 when out of range
-  int win_lo, win_len;        // fetch window: pc in [win_lo, win_lo + win_len) reads pre_s[pc]
+  int win_hi;                 // fetch window: pc in [0, win_hi) reads pre_s[pc]
   int cram_off;               // cart RAM offset of the bank at A000-BFFF; -1 when such
                               // accesses need the full path (disabled, absent, RTC)
   int rtc_sub, rtc_s, rtc_m, rtc_h, rtc_dl, rtc_dh;
@@ -300,11 +300,13 @@ struct Emu {
     // With bank 0 at offset 0 the bank-0 region fetches from it (minus the
     // boot ROM overlay and the last two bytes, whose instruction could reach
     // into bank N); with bank 1 also mapped the window spans both regions.
-    win_lo = bootrom ? 0x100 : 0;
+    // While the boot ROM overlays 0000-00FF the window is empty (a boot ROM
+    // runs inside its overlay, which the full fetch path serves anyway), so
+    // the window test is one unsigned compare.
     int hi = 0;
-    if (bank0_off == 0) hi = (bankN_off == 0 && pre_s_words >= 0x8000) ? 0x7FFE : 0x3FFE;
+    if (!bootrom && bank0_off == 0) hi = (bankN_off == 0 && pre_s_words >= 0x8000) ? 0x7FFE : 0x3FFE;
     if (hi > pre_s_words) hi = pre_s_words;  // only the staged words are in shared memory
-    win_len = hi > win_lo ? hi - win_lo : 0;
+    win_hi = hi;
     // A000-BFFF as plain bytes when it maps a whole bank of cart RAM
     // (ram_index / cart_read with RAM enabled and no RTC register selected)
     cram_off = -1;
@@ -1085,7 +1087,7 @@ __global__ void __launch_bounds__(MAXT, 1)
   h.clk = 0;
   h.next_ev = INT_MIN;  // EV_FIRST: the first instruction takes the exact tail
   int ninstr = 0;
-  int win_lo = s.win_lo, win_len = s.win_len, bankN_off = s.bankN_off, cram_off = s.cram_off;
+  int win_hi = s.win_hi, bankN_off = s.bankN_off, cram_off = s.cram_off;
   uint8_t* const mem = s.mem;
   uint8_t* const cram = s.cart_ram;
   auto save = [&]() {
@@ -1094,7 +1096,7 @@ __global__ void __launch_bounds__(MAXT, 1)
   auto load = [&]() {
     h.bcde = s.bcde; h.hlxa = s.hlxa; h.f = s.f; h.pc = s.pc; h.sp = s.sp; h.clk = s.clk;
     h.next_ev = s.next_ev;
-    win_lo = s.win_lo; win_len = s.win_len; bankN_off = s.bankN_off; cram_off = s.cram_off;
+    win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
   };
   // VRAM, WRAM and HRAM are plain bytes of the env's address space
   auto plain = [](int a) { return ((a >> 13) | 2) == 6 || (unsigned)(a - 0xFF80) < 0x7Fu; };
@@ -1113,14 +1115,14 @@ __global__ void __launch_bounds__(MAXT, 1)
     s.write_slow(a, v);  // ev is 0 here unless an earlier write of this instruction set it
     h.clk = s.clk;       // a timing write syncs (clk = 0) and sets ev
     if (s.ev) h.next_ev = INT_MIN;
-    win_lo = s.win_lo; win_len = s.win_len; bankN_off = s.bankN_off; cram_off = s.cram_off;
+    win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
   };
 
   while (run) {
     // ---- fetch + decode ----
     const int pc = h.pc;
     uint32_t w;
-    if ((unsigned)(pc - win_lo) < (unsigned)win_len) {
+    if ((unsigned)pc < (unsigned)win_hi) {
       w = pre_s[pc];
     } else if ((unsigned)(pc - 0x4000) < 0x3FFEu && bankN_off >= 0) {
       const int idx = pc + bankN_off;
