@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gbx|reference]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
 
-Workload ("config 2"): synthetic seeded ROM with the
+Workload (config 2 of the five benchmark configs): synthetic seeded ROM with the
 PPU on (LCDC=0xE3), 4,096 envs per GPU, 24 frames per env-step, release after
 8 frames, uniform actions from the 9-action codec (seed 0 + rank), and the
 72x20 packed 2-bpp observation rendered every step. Envs are independent, so
@@ -319,7 +319,7 @@ def run_gbx(args) -> None:
 
 
 def run_rollout_workload(args) -> None:
-    """policy rollouts on the MBC3 + PPU cartridge.
+    """Benchmark config 5: policy rollouts on the MBC3 + PPU cartridge.
 
     Per env-step: packed render -> 2 bpp unpack -> bf16 conv policy -> sampled
     actions -> step_torch -> masked restore of a seeded 5 % of envs from a

@@ -8,7 +8,7 @@ loop over ``GbxVecCudaBackend``: frames go from libgbx's packed buffer to the
 policy without leaving the GPU, and every tensor stays on the backend's
 device and current stream.
 
-``PixelPolicy`` is BASELINE's config-5 network: bf16
+``PixelPolicy`` is the config-5 benchmark network: bf16
 Conv(1->32, k4, s2) -> Conv(32->64, k3, s2) -> Conv(64->64, k3, s1) ->
 Linear(., 512) -> Linear(512, 9) with ReLUs, on frames scaled by 1/3 (the
 strides are not given by the benchmark; 2/2/1 are used).
