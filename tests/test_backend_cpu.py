@@ -5,12 +5,14 @@ when the backend is built, the reference's "not initialized" errors before
 
 from __future__ import annotations
 
+import re
+
 import numpy as np
 import pytest
 
 from gbxcule_b200 import GbxVecCudaBackend, roms
 
-NOT_INIT = "Backend not initialized. Call reset() first."
+NOT_INIT = re.escape("Backend not initialized. Call reset() first.")
 
 
 @pytest.fixture(scope="module")
