@@ -2,26 +2,41 @@
 """Benchmark: env-steps/s (frameskip 24) of the B200 Game Boy core.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gbx|reference]
+                    [--workload config5|config2] [--envs N]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
 
-Workload (config 2 of the five benchmark configs): synthetic seeded ROM with the
-PPU on (LCDC=0xE3), 4,096 envs per GPU, 24 frames per env-step, release after
-8 frames, uniform actions from the 9-action codec (seed 0 + rank), and the
-72x20 packed 2-bpp observation rendered every step. Envs are independent, so
+Default workload (config 5 of the five benchmark configs, the one the metric
+is quoted on): the MBC3 cartridge (64 x 16 KiB banks of seeded code, 32 KiB
+cart RAM, joypad jump table) with the PPU on (LCDC=0xE3, random tiles, maps
+and sprites), 131,072 envs per GPU, 24 frames per env-step, release after 8
+frames. Protocol: 600 warm-up frames (25 env-steps) of policy rollouts on
+every env, a golden snapshot of env 0, every env restored from it; then each
+env-step renders the 72x20 packed 2 bpp frames, unpacks them, runs the
+random-init bf16 conv policy, samples one action per env, steps every env
+and restores a seeded 5 % of envs from the snapshot. Envs are independent, so
 N GPUs run N independent env slices (weak scaling, no collective on the step
 path); ranks meet only for the barrier and the max-over-ranks timing.
 
+``--workload config2`` is the secondary line: config 2 (random-opcode loop,
+PPU on) at 4,096 envs per GPU with uniform random actions and the packed
+render every step.
+
 Prints one JSON line on rank 0:
-* value       env-steps/s of the whole job, inputs resident in HBM, step +
-              render kernels timed with CUDA events per step (L2 flushed
-              between timed steps), max over ranks;
-* e2e         the same through the public API with host buffers: actions
-              H2D from pinned memory and the packed frames D2H every step;
-* roofline    the step kernel's algorithmic HBM bytes per launch / its mean
-              event-timed duration vs the measured HBM peak (the kernel is
-              integer-issue/latency bound; the issue counters are in profiles/);
+* value        env-steps/s of the whole job, inputs resident in HBM, the whole
+               env-step (render, policy, sampling, step, restores) timed with
+               CUDA events on the launching stream, max over ranks;
+* e2e          the same loop through the public API with host buffers: each
+               step's reset mask copied in from pinned host memory, each
+               step's packed frames and sampled actions copied out;
+* roofline     the step kernel (gb_step_kernel, the dominant kernel) against
+               both roofs: integer issue (warp instructions issued per second
+               over the SMs' issue slots at the sampled clock; warp
+               instructions per emulated SM83 instruction from the committed
+               ncu capture) and HBM (algorithmic bytes per env-step, with the
+               emulated programs' RAM/IO bytes counted by the CPU oracle on a
+               sample of the same workload); ``bound`` names the larger;
 * cpu_baseline the CPU oracle (C restatement of the reference step) on the
-              host cores, on a bounded sample of the same workload.
+               host cores, on a bounded sample of the same workload.
 ``--impl reference`` times the reference's CPU implementation of the path;
 the reference's Warp runtime cannot be installed here, so that arm runs the
 oracle on all host threads over the same workload (kind "port").
@@ -44,36 +59,49 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-ENVS_PER_GPU = 4096
 FRAMES = 24
 RELEASE = 8
-CONFIG = 2
+WARMUP_FRAMES_STEPS = 25       # 600 frames before the golden snapshot (configs 4 and 5)
+RESTORE_RATE = 0.05
 METRIC = "env-steps/s (frameskip 24)"
 UNIT = "env-steps/s"
-WORKLOAD = "config2: PPU on (LCDC=0xE3) random-opcode loop, 4096 envs/GPU, frameskip 24, packed 72x20 obs"
+ISSUE_PER_SM_PER_CLOCK = 4     # one warp instruction per scheduler per cycle, 4 schedulers per SM
 
-# Algorithmic HBM bytes of one env-step of the step kernel (read + write of
-# every per-env field it owns, the action, the f32 obs vector). Instruction
-# RAM traffic is not counted, so this is a lower bound.
-STEP_STATE_BYTES = 2 * (27 * 4 + 2 * 8 + 3 + 20 * 4 + 12) + 4 + 32 * 4
-# dram__bytes_read.sum + dram__bytes_write.sum of one step-kernel launch on
-# this workload (4,096 envs), from an ncu --set full capture of
-# `bench.py --steps 3 --warmup 3 --no-cpu-baseline`. It includes the
-# emulated programs' RAM lines and the write-back of the L2 flush buffer
-# written just before the launch.
-STEP_KERNEL_DRAM_BYTES_4096 = 64.935168e6 + 146.290944e6
+WORKLOADS = {
+    "config5": dict(cfg=5, envs=131072, desc="config5: MBC3 + PPU cartridge (64 banks, 32 KiB cart RAM), "
+                    "{n} envs/GPU, frameskip 24, bf16 conv policy on packed frames, sampled actions, "
+                    "5 % masked restores per step from the snapshot after 600 warm-up frames"),
+    "config2": dict(cfg=2, envs=4096, desc="config2: PPU on (LCDC=0xE3) random-opcode loop, {n} envs/GPU, "
+                    "frameskip 24, uniform random actions, packed 72x20 obs rendered every step"),
+}
+
 # smsp__inst_executed.sum / emulated SM83 instructions of one step-kernel
-# launch on this workload, from the same ncu capture: the integer-issue cost
-# of one emulated instruction, used for the issue roofline below.
-WARP_INSTR_PER_EMULATED_INSTR = 48.096002450e9 / (4096 * 197327.3)
-SMS, ISSUE_PER_SM_PER_CLOCK = 148, 4
+# launch, from the committed ncu captures named beside each value (the
+# integer-issue cost of one emulated instruction at this workload's envs per
+# warp). tests/test_bench_cpu.py checks these against the profile summaries.
+WARP_INSTR_PER_EMULATED_INSTR = {
+    "config5": (None, "profiles/gb_step_kernel_config5_32768envs.md"),
+    "config2": (48.096002450e9 / (4096 * 197327.3), "profiles/gb_step_kernel_config2_4096envs.md"),
+}
+# dram__bytes_read.sum + dram__bytes_write.sum per env of one step-kernel
+# launch, from the same captures (None: not captured for this build).
+STEP_DRAM_BYTES_PER_ENV = {"config5": None, "config2": None}
+
+# Per-env state the step kernel reads at launch start and writes back at the
+# end (27 i32 + 2 i64 + 3 u8 scalars, 20 i32 cart_state words, 12 cached IO
+# ports), the action, and the f32 obs vector it writes.
+STATE_BYTES = 27 * 4 + 2 * 8 + 3 + 20 * 4 + 12
+ACTION_BYTES, OBS_VEC_BYTES = 4, 32 * 4
+R_OBS = 72 * 20                          # packed frame written by the render
+R_SRC = 8192 + 160 + 16                  # VRAM, OAM and LCD registers the render reads
+RESTORE_BYTES = {5: 65536 + 32768 + 1024 + 300, 2: 0}   # written per restored env
 
 
 def _peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured (MEASURED_PEAKS.json)"}
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
@@ -137,15 +165,6 @@ def _dist():
     return ws, rank, local
 
 
-def _issue_roofline(emu_instr_per_s_per_gpu: float, clk: dict) -> dict:
-    mhz = clk.get("sm_mhz") or 1965.0
-    peak = SMS * ISSUE_PER_SM_PER_CLOCK * mhz * 1e6
-    achieved = emu_instr_per_s_per_gpu * WARP_INSTR_PER_EMULATED_INSTR
-    return {"bound": "integer issue", "achieved": achieved, "peak": peak, "unit": "warp-instructions/s per GPU",
-            "frac": achieved / peak, "warp_instr_per_emulated_instr": WARP_INSTR_PER_EMULATED_INSTR,
-            "note": "warp instructions per emulated instruction from an ncu capture of this workload"}
-
-
 def _cpu_model() -> str:
     """Host CPU model name (Linux /proc/cpuinfo), recorded beside the CPU baseline."""
     try:
@@ -158,68 +177,303 @@ def _cpu_model() -> str:
     return "unknown"
 
 
-def cpu_oracle_rate(total_envs_hint: int, warmup: int, steps: int, threads: int, seed: int = 0) -> dict:
-    """Time the CPU oracle on a bounded sample of the workload (env-steps/s)."""
+def step_bytes(cfg: int, ram_ops_per_env_step: float, restore_rate: float) -> float:
+    """Algorithmic HBM bytes of one env-step of the step kernel (plus the render
+    and restore shares): action + per-env state read and written + the emulated
+    program's RAM/IO bytes (one per access, OAM DMA included) + packed frame
+    written + render source read + restored bytes."""
+    render = R_OBS + R_SRC
+    return (ACTION_BYTES + 2 * STATE_BYTES + OBS_VEC_BYTES + ram_ops_per_env_step + render
+            + restore_rate * RESTORE_BYTES.get(cfg, 0))
+
+
+def roofline(workload: str, cfg: int, envs: int, kernel_ms: float, emu_instr_per_launch: float,
+             ram_ops_per_env_step: float | None, sm_count: int, sm_mhz: float | None,
+             restore_rate: float) -> dict:
+    """Both roofs of the step kernel; ``bound`` is the one with the larger fraction."""
+    peaks = _peaks()
+    mhz = sm_mhz or 1965.0
+    secs = kernel_ms / 1e3
+    wipe, wsrc = WARP_INSTR_PER_EMULATED_INSTR[workload]
+    issue = None
+    if wipe:
+        ach = wipe * emu_instr_per_launch / secs
+        peak = sm_count * ISSUE_PER_SM_PER_CLOCK * mhz * 1e6
+        issue = {"achieved": ach / 1e9, "peak": peak / 1e9, "unit": "G warp-instructions/s", "frac": ach / peak,
+                 "warp_instr_per_emulated_instr": wipe, "source": wsrc,
+                 "peak_basis": f"{sm_count} SMs x {ISSUE_PER_SM_PER_CLOCK} issue slots x {mhz:.0f} MHz (sampled)"}
+    hbm = None
+    if ram_ops_per_env_step is not None:
+        b = step_bytes(cfg, ram_ops_per_env_step, restore_rate)
+        ach = b * envs / secs / 1e9
+        dram = STEP_DRAM_BYTES_PER_ENV.get(workload)
+        hbm = {"achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
+               "bytes_per_env_step": b, "ram_ops_bytes_per_env_step": ram_ops_per_env_step,
+               "peak_source": peaks["source"],
+               "traffic": None if dram is None else dram * envs}
+    cands = [(r["frac"], name, r) for name, r in (("integer-issue", issue), ("hbm", hbm)) if r]
+    if not cands:
+        return {"bound": None, "kernel": "gb_step_kernel", "kernel_ms": kernel_ms}
+    frac, name, r = max(cands, key=lambda t: t[0])
+    out = {"bound": name, "achieved": r["achieved"], "peak": r["peak"], "unit": r["unit"], "frac": frac,
+           "traffic": hbm["traffic"] if hbm else None, "kernel": "gb_step_kernel", "kernel_ms": kernel_ms,
+           "emulated_instr_per_launch": emu_instr_per_launch}
+    out["issue"] = issue
+    out["hbm"] = hbm
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle = C restatement of the reference step; test infrastructure)
+# ---------------------------------------------------------------------------
+def _oracle_leg(cfg: int, oracle, steps: int, rng, restore: bool, snap) -> float:
+    """``steps`` oracle env-steps (+ packed render, + restores); returns seconds."""
+    from gbxcule_b200 import roms
+
+    m = oracle.num_envs
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        oracle.step(roms.uniform_actions(rng, m, 9), FRAMES, RELEASE)
+        oracle.render_packed()
+        if restore:
+            oracle.restore(snap, (rng.random(m) < RESTORE_RATE).astype(np.uint8))
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_from_gpu(be, cfg: int, threads: int, seed: int = 0) -> dict:
+    """Time the CPU oracle on a bounded sample of the same workload, starting
+    from a contiguous block of the GPU batch's own current env states; also
+    count the emulated programs' RAM/IO bytes per env-step on that sample."""
     from gbxcule_b200 import roms
     from oracle import OracleEnvs
 
-    m = min(total_envs_hint, 48 * threads)
-    rom = roms.CONFIG_ROMS[CONFIG]()
-    o = OracleEnvs(rom, roms.boot_stub(), m, threads=threads)
+    m = min(be.num_envs, 24 * threads)
     rng = np.random.default_rng(seed)
-    for _ in range(warmup):
-        o.step(roms.uniform_actions(rng, m, 9), FRAMES, RELEASE)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        o.step(roms.uniform_actions(rng, m, 9), FRAMES, RELEASE)
-        o.render_packed()
-    dt = time.perf_counter() - t0
+    lo = int(rng.integers(0, be.num_envs - m + 1))
+    state = be.export_state(lo, lo + m)
+    o = OracleEnvs(roms.CONFIG_ROMS[cfg](), roms.boot_stub(), m, threads=threads, count_ram_ops=True)
+    for name, arr in state.items():
+        if name in o.s and not name.startswith("latch_"):
+            o.s[name][:] = np.asarray(arr).reshape(o.s[name].shape)
+    restore = cfg in (4, 5)
+    snap = o.snapshot(0)
+    steps = 2
+    dt = _oracle_leg(cfg, o, steps, rng, restore, snap)
+    ram_ops = float(o.ram_ops.sum()) / (m * steps)
+    what = "oracle step + packed render" + (" + 5 % masked restores" if restore else "")
     return {"value": m * steps / dt, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": _cpu_model(),
-            "sample": f"{m} envs x {steps} env-steps (after {warmup} warm-up steps) of the config-2 workload, "
-                      f"oracle step + packed render, {threads} threads, {dt:.1f} s"}
+            "sample": f"{m} envs (a contiguous block of the GPU batch, in its state after the timed steps) x "
+                      f"{steps} env-steps of the config-{cfg} workload: {what}; uniform random actions (the "
+                      f"policy is not part of the emulator baseline); {threads} threads, {dt:.1f} s",
+            "ram_ops_bytes_per_env_step": ram_ops}
+
+
+def reference_rate(cfg: int, threads: int, m: int, warmup: int, steps: int,
+                   warm_steps: int = WARMUP_FRAMES_STEPS) -> tuple[float, float, str]:
+    """The oracle on ``m`` envs from reset: the workload's warm-up (configs 4
+    and 5: ``warm_steps`` env-steps, snapshot of env 0, every env restored),
+    ``warmup`` untimed and ``steps`` timed env-steps. Returns (env-steps/s,
+    setup seconds, what one step does)."""
+    from gbxcule_b200 import roms
+    from oracle import OracleEnvs
+
+    o = OracleEnvs(roms.CONFIG_ROMS[cfg](), roms.boot_stub(), m, threads=threads)
+    rng = np.random.default_rng(0)
+    restore = cfg in (4, 5)
+    snap = None
+    t_setup = time.perf_counter()
+    if restore:
+        for _ in range(warm_steps):
+            o.step(roms.uniform_actions(rng, m, 9), FRAMES, RELEASE)
+        snap = o.snapshot(0)
+        o.restore(snap, np.ones(m, dtype=np.uint8))
+    _oracle_leg(cfg, o, warmup, rng, restore, snap)
+    t_setup = time.perf_counter() - t_setup
+    dt = _oracle_leg(cfg, o, steps, rng, restore, snap)
+    what = "oracle step + packed render" + (" + 5 % masked restores" if restore else "")
+    return m * steps / dt, t_setup, what
 
 
 def run_reference(args) -> None:
+    """The reference arm: the CPU restatement of the reference's step on all host
+    threads, the same workload from reset (warm-up, snapshot, restores)."""
     ws, rank, _ = _dist()
     if rank != 0:
         return
+    wl = WORKLOADS[args.workload]
+    cfg = wl["cfg"]
     threads = os.cpu_count() or 1
-    res = cpu_oracle_rate(ENVS_PER_GPU, args.warmup, args.steps, threads)
+    m = 4 * threads
+    value, t_setup, what = reference_rate(cfg, threads, m, args.warmup, args.steps)
+    warm = WARMUP_FRAMES_STEPS if cfg in (4, 5) else 0
     line = {
-        "impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": m / value * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "envs_per_gpu": ENVS_PER_GPU, "frameskip": FRAMES},
-        "cpu_baseline": res,
-        "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "reference Warp runtime is not installable offline; this arm is the C restatement of the "
+        "config": {"workload": wl["desc"].format(n=wl["envs"]), "envs_per_gpu": wl["envs"], "frameskip": FRAMES},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "cpu_model": _cpu_model(),
+                         "sample": f"each step: {m} envs x 1 env-step ({what}; uniform random actions, no "
+                                   f"policy) after {warm} warm-up env-steps, the snapshot and {args.warmup} "
+                                   f"untimed steps ({t_setup:.1f} s)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's Warp runtime is not installable offline; this arm is the C restatement of the "
                 "reference step (oracle/) on all host threads",
     }
     print(json.dumps(line), flush=True)
 
 
-def run_gbx(args) -> None:
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def _init_dist(timeout_s: int):
     import torch
 
-    from gbxcule_b200 import GbxVecCudaBackend, roms
-    from gbxcule_b200.multi import job_rate, rank_seed, reduce_run_stats
-
     ws, rank, local = _dist()
+    torch.cuda.set_device(local)
     dist = None
     if ws > 1:
         import datetime
 
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s),
                                 device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(local)
+    return dist, ws, rank, local
+
+
+def _finish(dist) -> None:
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_config5(args) -> None:
+    import torch
+
+    from gbxcule_b200 import GbxVecCudaBackend, ResetCache, roms
+    from gbxcule_b200.multi import job_rate, rank_seed, reduce_run_stats
+    from gbxcule_b200.rollout import make_policy, run_rollout
+
+    dist, ws, rank, local = _init_dist(600)
     dev = torch.device("cuda", local)
-    n = ENVS_PER_GPU
+    torch.backends.cudnn.benchmark = True  # the policy's conv shapes repeat every step
+    wl = WORKLOADS["config5"]
+    n = args.envs or wl["envs"]
     K, W = args.steps, args.warmup
-    rom = roms.CONFIG_ROMS[CONFIG]()
+    be = GbxVecCudaBackend(roms.config5_rom(), num_envs=n, frames_per_step=FRAMES,
+                           release_after_frames=RELEASE, render_on_step=False, device=f"cuda:{local}")
+    be.reset()
+    pol = make_policy(dev, seed=rank_seed(5, rank))
+    gen = torch.Generator(device=dev).manual_seed(rank_seed(1005, rank))
+    packed = torch.empty((n, 72, 20), dtype=torch.uint8, device=dev)
+    # protocol: 600 warm-up frames, golden snapshot of env 0, every env restored from it
+    run_rollout(be, pol, WARMUP_FRAMES_STEPS, generator=gen, packed_out=packed)
+    cache = ResetCache.from_backend(be, env_idx=0)
+    cache.apply_mask_torch(torch.ones(n, dtype=torch.bool, device=dev))
+    mrng = np.random.default_rng(rank_seed(2005, rank))
+    masks_host = (mrng.random((W + 2 * K, n)) < RESTORE_RATE).astype(np.uint8)
+    masks_dev = torch.as_tensor(masks_host[:W + K], device=dev)
+    run_rollout(be, pol, W, generator=gen, reset_cache=cache, reset_mask=lambda k: masks_dev[k], packed_out=packed)
+    i64 = be._view("i64")  # row 0: per-env emulated instruction counters
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ninstr0 = int(i64[0].sum())
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.perf_counter()
+    e0.record()
+    run_rollout(be, pol, K, generator=gen, reset_cache=cache, reset_mask=lambda k: masks_dev[W + k],
+                packed_out=packed, step_events=ev)
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    clk = clocks.stop()
+    total_ms = e0.elapsed_time(e1)
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    ninstr = int(i64[0].sum()) - ninstr0
+    k_used, k_settled = be.envs_per_warp()
+
+    # end to end through the public API with host buffers: the reset mask in
+    # from pinned memory, the packed frames and sampled actions out
+    mask_pin = torch.from_numpy(masks_host[W + K:]).pin_memory()
+    mask_dev = torch.empty((2, n), dtype=torch.uint8, device=dev)
+    host_out = (torch.empty((2, n, 72, 20), dtype=torch.uint8).pin_memory(),
+                torch.empty((2, n), dtype=torch.int32).pin_memory())
+
+    def e2e_mask(k):
+        mask_dev[k % 2].copy_(mask_pin[k], non_blocking=True)
+        return mask_dev[k % 2]
+
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    run_rollout(be, pol, K, generator=gen, reset_cache=cache, reset_mask=e2e_mask, packed_out=packed,
+                host_out=host_out)
+    f1.record()
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+
+    (total_ms, e2e_ms, step_avg_ms), (ninstr,) = reduce_run_stats(
+        dist, dev, [total_ms, e2e_ms, float(np.mean(step_ms))], [ninstr])
+    cpu = None
+    if ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_from_gpu(be, 5, os.cpu_count() or 1)
+    sm_count = be._info.sm_count
+    cache.close()
+    be.close()
+    _finish(dist)
+    if rank != 0:
+        return
+    value = job_rate(n, ws, K, total_ms)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
+        "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "u8", "data": "synthetic (seeded generated ROM, seeded restore masks, policy actions)",
+        "config": {"workload": wl["desc"].format(n=n), "envs_per_gpu": n, "frameskip": FRAMES,
+                   "release_after_frames": RELEASE, "restore_rate": RESTORE_RATE,
+                   "policy": "Conv(1-32,k4,s2)-Conv(32-64,k3,s2)-Conv(64-64,k3,s1)-Linear(512)-Linear(9), "
+                             "bf16, random init",
+                   "l2": "inputs larger than L2: 12.7 GB of per-env state per GPU (64 KiB address space + "
+                         "32 KiB cart RAM + 1 KiB serial per env), no flush",
+                   "parallelism": f"{ws} independent env slices, no collective on the step path",
+                   "envs_per_warp": k_used, "envs_per_warp_settled": k_settled},
+        "emulated_frames_per_s": value * FRAMES,
+        "emulated_instr_per_s": ninstr / (total_ms / 1e3),
+        "emulated_instr_per_env_step": ninstr / (n * ws * K),
+        "step_kernel_ms": step_avg_ms,
+        "e2e": {"value": job_rate(n, ws, K, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": n,
+                "d2h_bytes_per_step": n * (72 * 20 + 4)},
+        "roofline": roofline("config5", 5, n, step_avg_ms, ninstr / (ws * K),
+                             cpu["ram_ops_bytes_per_env_step"] if cpu else None, sm_count,
+                             clk.get("sm_mhz"), RESTORE_RATE),
+        "clocks": clk,
+        # libgbx kernels per timed step: render, step, masked restore (the
+        # policy's convolutions and sampling are torch/cuDNN kernels)
+        "gpu_launches": 3 * K,
+        "wall_s_timed": wall,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def run_config2(args) -> None:
+    import torch
+
+    from gbxcule_b200 import GbxVecCudaBackend, roms
+    from gbxcule_b200.multi import job_rate, rank_seed, reduce_run_stats
+
+    dist, ws, rank, local = _init_dist(120)
+    dev = torch.device("cuda", local)
+    wl = WORKLOADS["config2"]
+    n = args.envs or wl["envs"]
+    K, W = args.steps, args.warmup
+    rom = roms.config2_rom()
     rng = np.random.default_rng(rank_seed(0, rank))  # this rank's own env slice
     acts_host = np.stack([roms.uniform_actions(rng, n, 9) for _ in range(W + 2 * K)])
     be = GbxVecCudaBackend(rom, num_envs=n, frames_per_step=FRAMES, release_after_frames=RELEASE,
@@ -229,11 +483,14 @@ def run_gbx(args) -> None:
     for w in range(W):
         be.step_torch(acts_dev[w])
         be.render_pixels_snapshot_torch()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    # read-only L2 sweep between timed steps: evicts the previous step's lines
+    # (their write-back happens here, outside the timed region) and writes nothing
+    sweep = torch.ones(256 << 20, dtype=torch.uint8, device=dev)
+    sink = torch.empty((), dtype=torch.int64, device=dev)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    i64 = be._view("i64")  # row 0: per-env emulated instruction counters
+    i64 = be._view("i64")
     ninstr0 = int(i64[0].sum())
     clocks = ClockSampler(local)
     clocks.start()
@@ -241,7 +498,7 @@ def run_gbx(args) -> None:
            torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     wall0 = time.perf_counter()
     for k in range(K):
-        flush.zero_()  # L2 flush between timed steps, outside the events
+        torch.sum(sweep, dtype=torch.int64, out=sink)
         s, m, e = ev[k]
         s.record()
         be.step_torch(acts_dev[W + k])
@@ -254,8 +511,8 @@ def run_gbx(args) -> None:
     step_ms = [s.elapsed_time(m) for s, m, _ in ev]
     total_ms = sum(s.elapsed_time(e) for s, _, e in ev)
     ninstr = int(i64[0].sum()) - ninstr0
+    k_used, k_settled = be.envs_per_warp()
 
-    # end to end through the public API with host buffers
     acts_pin = torch.from_numpy(acts_host[W + K:W + 2 * K]).pin_memory()
     out_dev = torch.empty((n, 72, 20), dtype=torch.uint8, device=dev)
     out_host = torch.empty((2, n, 72, 20), dtype=torch.uint8).pin_memory()
@@ -276,115 +533,40 @@ def run_gbx(args) -> None:
 
     (total_ms, e2e_ms, step_avg_ms), (ninstr,) = reduce_run_stats(
         dist, dev, [total_ms, e2e_ms, float(np.mean(step_ms))], [ninstr])
+    cpu = None
+    if ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_from_gpu(be, 2, os.cpu_count() or 1)
+    sm_count = be._info.sm_count
     be.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    _finish(dist)
     if rank != 0:
         return
-    total_envs = n * ws
     value = job_rate(n, ws, K, total_ms)
-    peaks = _peaks()
-    achieved = STEP_STATE_BYTES * n / (step_avg_ms / 1e3) / 1e9
-    traffic = STEP_KERNEL_DRAM_BYTES_4096 * n / 4096
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
         "ms_per_step": total_ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u8", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "envs_per_gpu": n, "frameskip": FRAMES, "release_after_frames": RELEASE,
-                   "obs": "packed 2bpp 72x20 rendered every step", "l2": "flushed between timed steps (256 MiB write)",
-                   "parallelism": f"{ws} independent env slices, no collective on the step path"},
+        "dtype": "u8", "data": "synthetic (seeded generated ROM and actions)",
+        "config": {"workload": wl["desc"].format(n=n), "envs_per_gpu": n, "frameskip": FRAMES,
+                   "release_after_frames": RELEASE,
+                   "l2": "read-only 256 MiB sweep between timed steps (outside the events)",
+                   "parallelism": f"{ws} independent env slices, no collective on the step path",
+                   "envs_per_warp": k_used, "envs_per_warp_settled": k_settled},
         "emulated_frames_per_s": value * FRAMES,
-        # SM83 instructions retired by all envs per second of step-kernel time
-        # (the step kernel is bound by integer issue per emulated instruction)
         "emulated_instr_per_s": ninstr / (step_avg_ms * K / 1e3),
-        "emulated_instr_per_env_step": ninstr / (total_envs * K),
+        "emulated_instr_per_env_step": ninstr / (n * ws * K),
+        "step_kernel_ms": step_avg_ms,
         "e2e": {"value": job_rate(n, ws, K, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": 4 * n,
                 "d2h_bytes_per_step": 72 * 20 * n},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                     "peak_source": peaks["source"], "kernel": "gb_step_kernel",
-                     "kernel_ms": step_avg_ms, "bytes_per_env_step": STEP_STATE_BYTES},
-        # the binding roof: warp-instruction issue slots used by the step
-        # kernel (emulated instructions/s x warp instructions per emulated
-        # instruction) over the SMs' issue slots at the sampled SM clock
-        "issue_roofline": _issue_roofline(ninstr / (step_avg_ms * K / 1e3) / ws, clk),
+        "roofline": roofline("config2", 2, n, step_avg_ms, ninstr / (ws * K),
+                             cpu["ram_ops_bytes_per_env_step"] if cpu else None, sm_count,
+                             clk.get("sm_mhz"), 0.0),
         "clocks": clk,
-        "gpu_launches": 2 * K,
+        "gpu_launches": 2 * K,  # step + render per timed step
         "wall_s_timed": wall,
     }
-    if ws == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_oracle_rate(n, 3, 2, os.cpu_count() or 1)
+    if cpu:
+        line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
-
-
-def run_rollout_workload(args) -> None:
-    """Benchmark config 5: policy rollouts on the MBC3 + PPU cartridge.
-
-    Per env-step: packed render -> 2 bpp unpack -> bf16 conv policy -> sampled
-    actions -> step_torch -> masked restore of a seeded 5 % of envs from a
-    snapshot taken after warm-up. Timed end to end with CUDA events; the
-    policy and the restores are inside the timed region.
-    """
-    import torch
-
-    from gbxcule_b200 import GbxVecCudaBackend, ResetCache, roms
-    from gbxcule_b200.multi import job_rate, rank_seed, reduce_run_stats
-    from gbxcule_b200.rollout import make_policy, run_rollout
-
-    ws, rank, local = _dist()
-    dist = None
-    torch.cuda.set_device(local)
-    if ws > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.backends.cudnn.benchmark = True  # the policy's conv shapes repeat every step
-    n = args.envs or 131072
-    K, W = args.steps, args.warmup
-    be = GbxVecCudaBackend(roms.config5_rom(), num_envs=n, frames_per_step=FRAMES,
-                           release_after_frames=RELEASE, render_on_step=False, device=f"cuda:{local}")
-    be.reset()
-    pol = make_policy(dev, seed=rank_seed(5, rank))
-    gen = torch.Generator(device=dev).manual_seed(rank_seed(1005, rank))
-    packed = torch.empty((n, 72, 20), dtype=torch.uint8, device=dev)
-    run_rollout(be, pol, W, generator=gen, packed_out=packed)
-    cache = ResetCache.from_backend(be, env_idx=0)
-    masks = [torch.as_tensor(np.random.default_rng(rank_seed(2005, rank) + k).random(n) < 0.05, device=dev)
-             for k in range(K)]
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    clocks = ClockSampler(local)
-    clocks.start()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    run_rollout(be, pol, K, generator=gen, reset_cache=cache, reset_mask=lambda k: masks[k], packed_out=packed)
-    e1.record()
-    torch.cuda.synchronize()
-    clk = clocks.stop()
-    (ms,), _ = reduce_run_stats(dist, dev, [e0.elapsed_time(e1)], [])
-    cache.close()
-    be.close()
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
-    value = job_rate(n, ws, K, ms)
-    print(json.dumps({
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": K, "warmup": W,
-        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "u8", "data": "synthetic",
-        "config": {"workload": f"config5: MBC3 + PPU cartridge, {n} envs/GPU, frameskip 24, bf16 conv policy "
-                               "on packed frames, sampled actions, 5 % masked restores per step",
-                   "envs_per_gpu": n, "policy": "Conv(1-32,k4,s2)-Conv(32-64,k3,s2)-Conv(64-64,k3,s1)-"
-                   "Linear(512)-Linear(9), bf16, random init"},
-        "emulated_frames_per_s": value * FRAMES, "clocks": clk}), flush=True)
 
 
 def main() -> None:
@@ -394,18 +576,18 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="gbx", choices=["gbx", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config2", choices=["config2", "config5"],
-                    help="config2 (default): the benchmark line; config5: policy rollouts")
-    ap.add_argument("--envs", type=int, default=0, help="envs per GPU for --workload config5")
+    ap.add_argument("--workload", default="config5", choices=sorted(WORKLOADS),
+                    help="config5 (default): the benchmark line; config2: the secondary line")
+    ap.add_argument("--envs", type=int, default=0, help="envs per GPU (default: the workload's)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "config5":
-        run_rollout_workload(args)
+        run_config5(args)
     else:
-        run_gbx(args)
+        run_config2(args)
 
 
 if __name__ == "__main__":

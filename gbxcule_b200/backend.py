@@ -105,7 +105,8 @@ class GbxVecCudaBackend:
         self.num_actions = len(ACTION_CODECS[action_codec])
         self.device = "cuda"
         self._ordinal = int(str(device).split(":")[-1]) if str(device) != "cuda" else 0
-        self._lib = L.lib()
+        self._libh = None  # libgbx, loaded by the first reset() (building needs nvcc)
+        self._generation = 0  # bumped by reset() and close(); ResetCache checks it
         self._h = None
         self._initialized = False
         self._views: dict[str, Any] = {}
@@ -115,6 +116,12 @@ class GbxVecCudaBackend:
         self.obs_spec = ArraySpec((self.num_envs, obs_dim), "float32", "Observation vector per environment")
 
     # ------------------------------------------------------------------ helpers
+    @property
+    def _lib(self):
+        if self._libh is None:
+            self._libh = L.lib()
+        return self._libh
+
     def _torch(self):
         import torch
 
@@ -183,10 +190,13 @@ class GbxVecCudaBackend:
         return obs, {"seed": seed}
 
     def _free(self) -> None:
+        # Views handed out earlier stay valid: each holds its own reference to
+        # the old batch, whose memory is freed when the last of them goes.
         self._views.clear()
         if self._h is not None:
             self._lib.gbx_destroy(self._h)
             self._h = None
+            self._generation += 1
         self._initialized = False
 
     def close(self) -> None:
@@ -548,6 +558,18 @@ class GbxVecCudaBackend:
         self._view("i32")[L.I32_FIELDS.index("serial_len"), env_idx] = 0
         self._view("u8")[L.U8_FIELDS.index("serial_overflow"), env_idx] = 0
         return data
+
+    def envs_per_warp(self) -> tuple[int, bool]:
+        """(K of the latest step launch, whether K is settled) of the step kernel."""
+        self._need()
+        info = L.Info()
+        L.check(self._lib.gbx_get_info(self._h, ctypes.byref(info)))
+        return int(info.envs_per_warp), bool(info.envs_per_warp_tuned)
+
+    def set_envs_per_warp(self, k: int) -> None:
+        """Fix the step kernel's envs per warp (1..32), or 0 for the automatic choice."""
+        self._need()
+        L.check(self._lib.gbx_set_envs_per_warp(self._h, int(k)), "gbx_set_envs_per_warp")
 
     def device_status(self, clear: bool = False) -> int:
         """Device error bits (1: an env's mbc_kind differs from the cartridge)."""

@@ -7,6 +7,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <new>
 #include <string>
 
@@ -15,14 +16,17 @@
 
 namespace gbx {
 cudaError_t launch_step(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames, int release,
-                        int stage, cudaStream_t stream, const DebugCfg& dbg);
+                        int stage, cudaStream_t stream, const DebugCfg& dbg, int K, int sms);
+int fill_envs_per_warp(long long n, int sms);
+int envs_per_warp_override();
 cudaError_t launch_render_bg_env0(const DevState& st, uint8_t* out, cudaStream_t stream);
 void predecode_rom(const uint8_t* rom, int n, uint32_t* out);
 cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
                           cudaStream_t stream);
-cudaError_t launch_init(const DevState& st, cudaStream_t s);
+cudaError_t launch_init(const DevState& st, cudaStream_t s, int sms);
 cudaError_t launch_snapshot(const DevState& st, const Snapshot& snap, int env, cudaStream_t s);
-cudaError_t launch_restore(const DevState& st, const Snapshot& snap, const uint8_t* mask, cudaStream_t s);
+cudaError_t launch_restore(const DevState& st, const Snapshot& snap, const uint8_t* mask, cudaStream_t s,
+                           int sms);
 }  // namespace gbx
 
 using namespace gbx;
@@ -30,6 +34,24 @@ using namespace gbx;
 static_assert((int)GBX_I32_COUNT == (int)I32_COUNT, "i32 field table mismatch");
 static_assert((int)GBX_I64_COUNT == (int)I64_COUNT, "i64 field table mismatch");
 static_assert((int)GBX_U8_COUNT == (int)U8_COUNT, "u8 field table mismatch");
+
+// Envs per warp (K) of the step kernel, chosen per handle. K only changes
+// which lanes run which envs, never a result. Automatic mode times its
+// candidates on the handle's first real steps, in the order A B B A (or
+// A B C C B A) so that a step time drifting as the envs diverge weighs on
+// every candidate alike, and keeps the fastest. Timing uses events around the
+// step launches already requested; no step is added or repeated.
+struct KTuner {
+  static constexpr int MAXC = 3;
+  int fixed = 0;              // > 0: K set by the caller or GBX_ENVS_PER_WARP
+  int ncand = 0, cand[MAXC] = {0, 0, 0};
+  int order[2 * MAXC] = {0, 0, 0, 0, 0, 0};
+  int launched = 0;           // trials launched (events recorded)
+  int measured = 0;           // trials whose events were read
+  float ms[MAXC] = {0, 0, 0};
+  cudaEvent_t ev[2 * MAXC][2] = {};
+  int best = 0;               // chosen K once every trial is measured
+};
 
 struct gbx_env {
   DevState st;
@@ -42,6 +64,12 @@ struct gbx_env {
   uint8_t* frame_bg;       // env-0 160x144 frame
   DebugCfg dbg;            // debug traps (all off by default)
   bool initialized;
+  int sm_count;            // SMs of the handle's device
+  KTuner tune;
+  int last_k;              // K of the latest step launch
+  // Owners: the creator (dropped by gbx_destroy) plus one per live DLPack
+  // tensor (dropped by its deleter). Device memory is freed with the last.
+  std::atomic<int> refs;
 };
 
 struct gbx_snapshot {
@@ -132,6 +160,43 @@ void free_env(gbx_env* h) {
                   h->frame_bg};
   for (void* p : ptrs)
     if (p) cudaFree(p);
+  for (auto& pair : h->tune.ev)
+    for (cudaEvent_t& e : pair)
+      if (e) cudaEventDestroy(e);
+}
+
+// Candidates of the automatic K choice for n envs on `sms` SMs: the K that
+// fills one wave of warps, half of it (two waves of emptier warps) and 32.
+void tuner_init(KTuner& t, int n, int sms, int fixed) {
+  t = KTuner();
+  t.fixed = fixed;
+  const int kf = fill_envs_per_warp(n, sms);
+  t.cand[t.ncand++] = kf;
+  if (kf > 1) t.cand[t.ncand++] = kf / 2;
+  if (kf < 32) t.cand[t.ncand++] = 32;
+  for (int i = 0; i < t.ncand; i++) {
+    t.order[i] = i;
+    t.order[2 * t.ncand - 1 - i] = i;
+  }
+  t.best = kf;
+}
+
+// Read the events of finished trials; once all are read, keep the fastest K.
+void tuner_poll(KTuner& t) {
+  while (t.measured < t.launched) {
+    cudaEvent_t* e = t.ev[t.measured];
+    if (cudaEventQuery(e[1]) != cudaSuccess) { cudaGetLastError(); return; }  // not finished yet
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, e[0], e[1]) != cudaSuccess) { cudaGetLastError(); ms = 1e30f; }
+    t.ms[t.order[t.measured]] += ms;
+    t.measured++;
+  }
+  if (t.measured == 2 * t.ncand) {
+    int b = 0;
+    for (int i = 1; i < t.ncand; i++)
+      if (t.ms[i] < t.ms[b]) b = i;
+    t.best = t.cand[b];
+  }
 }
 
 int zero_state(gbx_env* h, cudaStream_t s) {
@@ -152,6 +217,16 @@ int zero_state(gbx_env* h, cudaStream_t s) {
   if (h->pix) CK(cudaMemsetAsync(h->pix, 0, (size_t)SHADE_BYTES * st.n, s), "memset pix");
   if (h->pix_packed) CK(cudaMemsetAsync(h->pix_packed, 0, (size_t)PACKED_BYTES * st.n, s), "memset pix_packed");
   return GBX_OK;
+}
+
+// Drop one owner; the last one frees every device buffer. cudaFree waits for
+// the device's outstanding work, as the callers' declarations state.
+void env_release(gbx_env* h) {
+  if (h->refs.fetch_sub(1, std::memory_order_acq_rel) != 1) return;
+  DeviceGuard g(h->cfg.device);
+  cudaDeviceSynchronize();
+  free_env(h);
+  delete h;
 }
 
 int check_env(const gbx_env* h) {
@@ -220,7 +295,7 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
   DeviceGuard g(cfg->device);
   gbx_env* h = new (std::nothrow) gbx_env();
   if (!h) return fail(GBX_ERR_OOM, "host allocation failed");
-  memset(h, 0, sizeof *h);
+  h->refs.store(1);
   h->cfg = *cfg;
   DevState& st = h->st;
   st.n = cfg->num_envs;
@@ -275,16 +350,21 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
     delete h;
     return cuda_fail(e, "upload ROM");
   }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device) != cudaSuccess || sms <= 0) {
+    free_env(h);
+    delete h;
+    return fail(GBX_ERR_CUDA, "cannot read the SM count of device %d", cfg->device);
+  }
+  h->sm_count = sms;
+  tuner_init(h->tune, st.n, sms, envs_per_warp_override());
   *out = h;
   return GBX_OK;
 }
 
 int gbx_destroy(gbx_env* h) {
   if (!h) return GBX_OK;
-  DeviceGuard g(h->cfg.device);
-  cudaDeviceSynchronize();
-  free_env(h);
-  delete h;
+  env_release(h);
   return GBX_OK;
 }
 
@@ -301,6 +381,10 @@ int gbx_get_info(const gbx_env* h, gbx_info* out) {
   out->rom_bank_mask = h->st.rom_bank_mask;
   out->ram_bank_count = h->st.ram_bank_count;
   out->ram_bytes = h->ram_bytes;
+  out->sm_count = h->sm_count;
+  if (!h->tune.fixed) tuner_poll(const_cast<gbx_env*>(h)->tune);  // trials that have finished since
+  out->envs_per_warp = h->tune.fixed ? h->tune.fixed : h->last_k ? h->last_k : h->tune.best;
+  out->envs_per_warp_tuned = h->tune.fixed ? 1 : h->tune.measured == 2 * h->tune.ncand;
   return GBX_OK;
 }
 
@@ -309,11 +393,13 @@ int gbx_reset(gbx_env* h, void* stream) {
   DeviceGuard g(h->cfg.device);
   cudaStream_t s = S_(stream);
   RET(zero_state(h, s));
-  CK(launch_init(h->st, s), "init kernel");
+  CK(launch_init(h->st, s, h->sm_count), "init kernel");
   h->initialized = true;
   if (h->cfg.stage == STAGE_OBS || h->cfg.stage == STAGE_FULL) {
     const int32_t* zero_actions = h->st.i32 + (size_t)F_ACTIONS * h->st.S;
-    CK(launch_step(h->st, h->pre, zero_actions, 0, 0, h->cfg.stage, s, h->dbg), "step kernel (reset obs)");
+    const int K = h->tune.fixed ? h->tune.fixed : h->tune.best;
+    CK(launch_step(h->st, h->pre, zero_actions, 0, 0, h->cfg.stage, s, h->dbg, K, h->sm_count),
+       "step kernel (reset obs)");
   }
   return GBX_OK;
 }
@@ -324,7 +410,44 @@ int gbx_step(gbx_env* h, const int32_t* actions, int32_t frames, int32_t release
   if (frames < 0) return fail(GBX_ERR_INVALID, "frames_to_run must be >= 0, got %d", frames);
   if (frames > 25000) return fail(GBX_ERR_INVALID, "frames_to_run %d exceeds 25000 per launch", frames);
   DeviceGuard g(h->cfg.device);
-  CK(launch_step(h->st, h->pre, actions, frames, release, h->cfg.stage, S_(stream), h->dbg), "step kernel");
+  cudaStream_t s = S_(stream);
+  KTuner& t = h->tune;
+  int K = t.fixed;
+  cudaEvent_t* trial = nullptr;
+  if (!K) {
+    tuner_poll(t);
+    K = t.best;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    // trials only on real steps, outside stream capture and debug traps
+    if (t.launched < 2 * t.ncand && frames > 0 && !h->dbg.active() &&
+        cudaStreamIsCapturing(s, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone) {
+      trial = t.ev[t.launched];
+      for (int k = 0; k < 2; k++)
+        if (!trial[k]) CK(cudaEventCreate(&trial[k]), "tuner event");
+      K = t.cand[t.order[t.launched]];
+      CK(cudaEventRecord(trial[0], s), "tuner event record");
+    }
+  }
+  h->last_k = K;
+  CK(launch_step(h->st, h->pre, actions, frames, release, h->cfg.stage, s, h->dbg, K, h->sm_count),
+     "step kernel");
+  if (trial) {
+    CK(cudaEventRecord(trial[1], s), "tuner event record");
+    t.launched++;
+  }
+  return GBX_OK;
+}
+
+int gbx_set_envs_per_warp(gbx_env* h, int32_t k) {
+  RET(check_env(h));
+  if (k < 0 || k > 32) return fail(GBX_ERR_INVALID, "envs_per_warp must be in [0, 32], got %d", k);
+  DeviceGuard g(h->cfg.device);
+  cudaDeviceSynchronize();  // no trial of the previous setting is still in flight
+  KTuner fresh;
+  tuner_init(fresh, h->st.n, h->sm_count, k);
+  for (int i = 0; i < 2 * KTuner::MAXC; i++)  // keep the created events
+    for (int j = 0; j < 2; j++) fresh.ev[i][j] = h->tune.ev[i][j];
+  h->tune = fresh;
   return GBX_OK;
 }
 
@@ -407,7 +530,7 @@ int gbx_masked_restore(gbx_env* h, const gbx_snapshot* sn, const uint8_t* mask, 
   if (sn->device != h->cfg.device || sn->s.ram_bytes != h->ram_rows)
     return fail(GBX_ERR_INVALID, "snapshot belongs to a different env batch");
   DeviceGuard g(h->cfg.device);
-  CK(launch_restore(h->st, sn->s, mask, S_(stream)), "restore kernel");
+  CK(launch_restore(h->st, sn->s, mask, S_(stream), h->sm_count), "restore kernel");
   return GBX_OK;
 }
 
@@ -446,7 +569,13 @@ int gbx_buffer(const gbx_env* h, int32_t which, gbx_buffer_info* o) {
   return GBX_OK;
 }
 
-static void dl_deleter(DLManagedTensor* t) { free(t); }
+// A DLPack tensor owns a reference to its handle (manager_ctx), so a view
+// held past gbx_destroy keeps the device memory it aliases alive.
+static void dl_deleter(DLManagedTensor* t) {
+  gbx_env* h = static_cast<gbx_env*>(t->manager_ctx);
+  free(t);
+  if (h) env_release(h);
+}
 
 int gbx_export_dlpack(const gbx_env* h, int32_t which, void** out) {
   if (!out) return fail(GBX_ERR_INVALID, "null out");
@@ -469,7 +598,8 @@ int gbx_export_dlpack(const gbx_env* h, int32_t which, void** out) {
   t->dl_tensor.shape = shape;
   t->dl_tensor.strides = strides;
   t->dl_tensor.byte_offset = 0;
-  t->manager_ctx = nullptr;
+  const_cast<gbx_env*>(h)->refs.fetch_add(1, std::memory_order_relaxed);
+  t->manager_ctx = const_cast<gbx_env*>(h);
   t->deleter = dl_deleter;
   *out = t;
   return GBX_OK;

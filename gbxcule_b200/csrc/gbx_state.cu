@@ -113,8 +113,8 @@ __global__ void __launch_bounds__(RESTORE_THREADS) restore_kernel(DevState st, S
 }
 
 // --- launchers ---------------------------------------------------------------------
-cudaError_t launch_init(const DevState& st, cudaStream_t s) {
-  init_kernel<<<148 * 4, 256, 0, s>>>(st);
+cudaError_t launch_init(const DevState& st, cudaStream_t s, int sms) {
+  init_kernel<<<(sms > 0 ? sms : 1) * 4, 256, 0, s>>>(st);
   return cudaGetLastError();
 }
 
@@ -123,10 +123,12 @@ cudaError_t launch_snapshot(const DevState& st, const Snapshot& snap, int env, c
   return cudaGetLastError();
 }
 
-cudaError_t launch_restore(const DevState& st, const Snapshot& snap, const uint8_t* mask, cudaStream_t s) {
+cudaError_t launch_restore(const DevState& st, const Snapshot& snap, const uint8_t* mask, cudaStream_t s,
+                           int sms) {
   // 8 resident 256-thread blocks per SM; fewer blocks than envs keeps the
   // mask scan cheap when few envs are masked
-  const int blocks = st.n < 148 * 8 ? st.n : 148 * 8;
+  const int slots = (sms > 0 ? sms : 1) * 8;
+  const int blocks = st.n < slots ? st.n : slots;
   restore_kernel<<<blocks, RESTORE_THREADS, 0, s>>>(st, snap, mask);
   return cudaGetLastError();
 }

@@ -1503,18 +1503,31 @@ static int env_int(const char* name, int dflt) {
   return v && *v ? atoi(v) : dflt;
 }
 
-// Envs per warp for a batch of n envs (GBX_ENVS_PER_WARP overrides).
-// One env per warp has no divergence but leaves 31 lanes idle, so its
-// throughput stops growing once every SM holds a full wave of single-env
-// warps; 32 envs per warp shares every issue slot among the envs that take
-// the same path and keeps growing with n. Measured on B200 (config ROMs,
-// frameskip 24): 4,096 envs run fastest at K = 1, 16,384 and 65,536 at
-// K = 32, intermediate K never beats both. Switch after three waves.
-int step_envs_per_warp(int n) {
-  int k = env_int("GBX_ENVS_PER_WARP", 0);
-  if (k > 0) return k > 32 ? 32 : k;
-  const long long wave = 148LL * 28;  // resident single-env warps per GPU at this kernel's footprint
-  return n <= 3 * wave ? 1 : 32;
+// Largest number of this kernel's warps one SM holds: one block per SM (the
+// staged ROM words fill shared memory) of at most 1024 threads.
+constexpr int WARPS_PER_SM = 32;
+
+// Envs per warp that fills the GPU with one wave of warps: the smallest K in
+// {1, 2, 4, 8, 16, 32} with ceil(n / K) <= sms * WARPS_PER_SM. A warp's time
+// per step is set by the dependent chain of its interpreter loop and grows
+// only slowly with the warps sharing its SM, so one full wave of warps
+// beats both fewer, fuller warps and a second wave. Measured on B200
+// (config-4 cartridge, frameskip 24): 65,536 envs 479 ms at K = 16 vs 522 ms
+// at K = 32 and 713 ms at K = 8; 16,384 envs 233 ms at K = 4 vs 326 ms at
+// K = 1 and 456 ms at K = 32. A HALT-heavy program can prefer K = 32 instead
+// (config 3 at 16,384 envs: 25-44 ms at K = 32, 64-112 ms at K = 4), which is
+// why the caller times the candidates on its first steps.
+int fill_envs_per_warp(long long n, int sms) {
+  const long long slots = (long long)(sms > 0 ? sms : 1) * WARPS_PER_SM;
+  int k = 1;
+  while (k < 32 && (n + k - 1) / k > slots) k <<= 1;
+  return k;
+}
+
+// GBX_ENVS_PER_WARP (1..32) fixes K for every handle; 0 or unset = automatic.
+int envs_per_warp_override() {
+  const int k = env_int("GBX_ENVS_PER_WARP", 0);
+  return k <= 0 ? 0 : k > 32 ? 32 : k;
 }
 
 template <int MBC, int MAXT, bool DBG>
@@ -1531,12 +1544,14 @@ static cudaError_t launch_t(const DevState& st, const uint32_t* pre, const int32
 
 template <int MBC>
 static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames,
-                              int release, int stage, cudaStream_t stream, const DebugCfg& dbg) {
-  const int K = step_envs_per_warp(st.n);
+                              int release, int stage, cudaStream_t stream, const DebugCfg& dbg, int K,
+                              int sms) {
+  K = K < 1 ? 1 : K > 32 ? 32 : K;
+  sms = sms < 1 ? 1 : sms;
   const long long warps = (st.n + K - 1) / K;
   // one block per SM (the pre-decoded banks fill shared memory): spread warps
-  int per_block = (int)((warps + 147) / 148);
-  per_block = per_block < 1 ? 1 : per_block > 32 ? 32 : per_block;
+  int per_block = (int)((warps + sms - 1) / sms);
+  per_block = per_block < 1 ? 1 : per_block > WARPS_PER_SM ? WARPS_PER_SM : per_block;
   const int threads = per_block * 32;
   const int blocks = (int)((warps + per_block - 1) / per_block);
   int stage_words = env_int("GBX_ROM_SMEM_WORDS", ROM_SMEM_MAX);  // experiments: staged ROM size
@@ -1556,12 +1571,13 @@ static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int
                                     rom_words, sm, dbg);
 }
 
+// K = envs per warp (1..32), sms = the device's SM count.
 cudaError_t launch_step(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames, int release,
-                        int stage, cudaStream_t stream, const DebugCfg& dbg) {
+                        int stage, cudaStream_t stream, const DebugCfg& dbg, int K, int sms) {
   switch (st.mbc_kind) {
-    case MBC_MBC1: return launch_mbc<MBC_MBC1>(st, pre, actions, frames, release, stage, stream, dbg);
-    case MBC_MBC3: return launch_mbc<MBC_MBC3>(st, pre, actions, frames, release, stage, stream, dbg);
-    default: return launch_mbc<MBC_ROM_ONLY>(st, pre, actions, frames, release, stage, stream, dbg);
+    case MBC_MBC1: return launch_mbc<MBC_MBC1>(st, pre, actions, frames, release, stage, stream, dbg, K, sms);
+    case MBC_MBC3: return launch_mbc<MBC_MBC3>(st, pre, actions, frames, release, stage, stream, dbg, K, sms);
+    default: return launch_mbc<MBC_ROM_ONLY>(st, pre, actions, frames, release, stage, stream, dbg, K, sms);
   }
 }
 

@@ -24,7 +24,7 @@ class ResetCache:
         self.num_envs = int(backend.num_envs)
         self.env_idx = env_idx
         self._snap = snap
-        self._handle = backend._h
+        self._generation = backend._generation
 
     @classmethod
     def from_backend(cls, backend: Any, *, env_idx: int = 0) -> "ResetCache":
@@ -56,7 +56,7 @@ class ResetCache:
         else:
             raise ValueError("mask must be bool or uint8")
         mask_u8 = mask_u8.contiguous()
-        if backend._h is None or backend._h.value != self._handle.value:
+        if backend._h is None or backend._generation != self._generation:
             raise RuntimeError("ResetCache belongs to a backend that was reset or closed")
         L.check(L.lib().gbx_masked_restore(backend._h, self._snap, ctypes.c_void_p(mask_u8.data_ptr()),
                                            backend._stream()), "gbx_masked_restore")

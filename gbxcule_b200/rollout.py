@@ -107,12 +107,17 @@ class Rollout:
 
 def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 16384,
                 reset_cache=None, reset_mask: Callable[[int], Any] | None = None,
-                packed_out=None) -> Rollout:
+                packed_out=None, step_events=None, host_out=None) -> Rollout:
     """``steps`` env-steps of render -> unpack -> policy -> sample -> step.
 
-    ``reset_mask(k)`` (a CUDA bool [N] or None) selects envs restored from
-    ``reset_cache`` after step k. The policy runs in chunks of ``chunk`` envs
-    to bound activation memory. Returns the sampled actions (and masks).
+    ``reset_mask(k)`` (a CUDA bool/uint8 [N] or None) selects envs restored
+    from ``reset_cache`` after step k. The policy runs in chunks of ``chunk``
+    envs to bound activation memory. ``step_events[k]`` (a pair of CUDA
+    events, optional) is recorded around step k's ``step_torch``.
+    ``host_out`` (optional pair of pinned host tensors, [2, N, 72, 20] uint8
+    and [2, N] int32) receives each step's packed frames and sampled actions,
+    copied asynchronously into slot k % 2. Returns the sampled actions (and
+    masks).
     """
     import torch
 
@@ -128,7 +133,14 @@ def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 163
                 hi = min(n, lo + chunk)
                 logits = policy(unpack_2bpp_u8(packed[lo:hi])).float()
                 acts[lo:hi] = torch.multinomial(torch.softmax(logits, dim=-1), 1, generator=generator)[:, 0].to(torch.int32)
+            if host_out is not None:
+                host_out[0][k % 2].copy_(packed, non_blocking=True)
+                host_out[1][k % 2].copy_(acts, non_blocking=True)
+            if step_events is not None:
+                step_events[k][0].record()
             backend.step_torch(acts)
+            if step_events is not None:
+                step_events[k][1].record()
             out.actions.append(acts)
             mask = reset_mask(k) if reset_mask is not None else None
             if mask is not None and reset_cache is not None:

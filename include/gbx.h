@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define GBX_ABI_VERSION 2
+#define GBX_ABI_VERSION 3
 
 typedef enum {
   GBX_OK = 0,
@@ -86,6 +86,9 @@ typedef struct {
   int32_t num_envs, env_stride, device, stage;
   int32_t mbc_kind;              /* 0 ROM only, 1 MBC1, 2 MBC3 */
   int32_t rom_bytes, rom_bank_count, rom_bank_mask, ram_bank_count, ram_bytes;
+  int32_t sm_count;              /* SMs of the device */
+  int32_t envs_per_warp;         /* K of the latest step launch (see gbx_set_envs_per_warp) */
+  int32_t envs_per_warp_tuned;   /* 1 once K is fixed or the automatic choice is made */
 } gbx_info;
 
 typedef struct {
@@ -127,7 +130,11 @@ const char* gbx_last_error(void);
  * (warp_vec.py:1188-1232). */
 int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const uint8_t* boot,
                size_t boot_len, gbx_env** out);
-/* Free every device buffer (warp_vec.py:1076-1141). NULL is a no-op. */
+/* Release the caller's ownership of the batch (warp_vec.py:1076-1141). NULL is
+ * a no-op. The handle must not be used afterwards. Device buffers are freed
+ * when the last owner goes: this call, or the deleter of the last DLPack
+ * tensor from gbx_export_dlpack still alive. The free synchronises the whole
+ * device (cudaDeviceSynchronize), not only one stream. */
 int gbx_destroy(gbx_env* env);
 int gbx_get_info(const gbx_env* env, gbx_info* out);
 
@@ -143,6 +150,17 @@ int gbx_reset(gbx_env* env, void* stream);
 int gbx_step(gbx_env* env, const int32_t* actions, int32_t frames_to_run,
              int32_t release_after_frames, void* stream);
 
+/* Envs per warp K of the step kernel: 1..32 fixes it, 0 = automatic (the
+ * default; GBX_ENVS_PER_WARP in the environment fixes it for every handle).
+ * No counterpart in the reference, whose Warp launch maps one env per thread
+ * with Warp's own block size. K never changes a result, only speed. In
+ * automatic mode the first 4 or 6 real steps of the handle each run with one
+ * of up to three candidates (the K that fills one wave of warps on the
+ * device, half of it, and 32), timed with CUDA events around the launches
+ * the caller requested, and later steps use the fastest. Synchronises the
+ * device. */
+int gbx_set_envs_per_warp(gbx_env* env, int32_t envs_per_warp);
+
 /* Snapshot renderer (ppu_render_downsampled.py:207-234 packed, :182-204 unpacked)
  * from current memory. out: device buffer of at least base_offset + n*1440 bytes
  * (packed) or n*5760 (unpacked); NULL renders into the env's own
@@ -155,6 +173,7 @@ int gbx_render_shades(gbx_env* env, uint8_t* out, void* stream);
 /* Capture env env_idx into a device snapshot (ResetCache.from_backend,
  * src/gbxcule/core/reset_cache.py:67-190). Enqueued on stream. */
 int gbx_snapshot_create(gbx_env* env, int32_t env_idx, void* stream, gbx_snapshot** out);
+/* Free a snapshot. Synchronises the whole device (cudaDeviceSynchronize) first. */
 int gbx_snapshot_destroy(gbx_snapshot* snap);
 /* Restore every env whose mask byte is non-zero from the snapshot
  * (ResetCache.apply_mask_torch, reset_cache.py:192-307,381-411). mask: device
@@ -164,8 +183,9 @@ int gbx_masked_restore(gbx_env* env, const gbx_snapshot* snap, const uint8_t* ma
 /* Describe a device buffer for a zero-copy view (memory_torch / pixels_torch /
  * pixels_packed_torch, warp_vec.py:799-901). */
 int gbx_buffer(const gbx_env* env, int32_t which, gbx_buffer_info* out);
-/* Same buffer as a DLPack v0 DLManagedTensor* (written to *out). The consumer
- * calls its deleter; the memory stays owned by the env. */
+/* Same buffer as a DLPack v0 DLManagedTensor* (written to *out). The tensor
+ * owns a reference to the batch (manager_ctx): its memory stays valid until
+ * the consumer calls the deleter, even after gbx_destroy. */
 int gbx_export_dlpack(const gbx_env* env, int32_t which, void** out);
 
 /* Synchronous copies between device state and host buffers in the reference's

@@ -59,7 +59,7 @@ class _Ctx(ctypes.Structure):
                              "tima_reload_delay", "ppu_scanline_cycle", "ppu_ly",
                              "ppu_window_line", "ppu_stat_prev")]
         + [("latch", _P * 9), ("reward_out", _P), ("obs_out", _P),
-           ("stage", ctypes.c_int32), ("num_envs", ctypes.c_int32)]
+           ("stage", ctypes.c_int32), ("num_envs", ctypes.c_int32), ("ram_ops", _P)]
     )
 
 
@@ -93,7 +93,7 @@ class OracleEnvs:
     """A batch of emulated consoles stepped by the C oracle."""
 
     def __init__(self, rom: bytes, boot: bytes, num_envs: int, *, stage: str = "obs_only",
-                 threads: int | None = None) -> None:
+                 threads: int | None = None, count_ram_ops: bool = False) -> None:
         self.rom, self.spec = cart.load_rom(rom)
         if len(boot) != 0x100:
             raise ValueError("boot ROM must be 256 bytes")
@@ -101,6 +101,9 @@ class OracleEnvs:
         self.num_envs = int(num_envs)
         self.stage = stage
         self.threads = threads or os.cpu_count() or 1
+        # per-env RAM/IO bytes touched by the emulated instructions (gbx_oracle.c
+        # gbxo_ctx.ram_ops), accumulated over every step when enabled
+        self.ram_ops = np.zeros(self.num_envs, dtype=np.int64) if count_ram_ops else None
         from gbxcule_b200.debug_traps import read_debug_env
 
         # the reference reads its debug-trap variables when the backend is built
@@ -151,6 +154,7 @@ class OracleEnvs:
         c.reward_out, c.obs_out = _ptr(s["reward"]), _ptr(s["obs"])
         c.stage = STAGES[self.stage]
         c.num_envs = self.num_envs
+        c.ram_ops = _ptr(self.ram_ops) if self.ram_ops is not None else None
         return c
 
     def _run(self, frames: int, release: int, lo: int = 0, hi: int | None = None) -> None:

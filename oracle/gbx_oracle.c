@@ -67,6 +67,13 @@ typedef struct {
     uint8_t *latch[9]; /* lcdc scx scy bgp wx wy win_line obp0 obp1, u8[144] */
     float *reward_out, *obs_out;
     int32_t stage, num_envs;
+    /* optional (NULL = off): per env, bytes of RAM/IO (0x8000-0xFFFF, cart RAM
+     * included) read or written by the emulated instructions, OAM DMA copies
+     * counted as 160 read + 160 written. ROM and boot-ROM reads are not
+     * counted (instruction fetch and ROM data: shared, read-only). Measures
+     * the M_ops + D_dma terms of the step's algorithmic bytes; no effect on
+     * the emulation. */
+    int64_t *ram_ops;
 } gbxo_ctx;
 
 typedef struct {
@@ -261,6 +268,7 @@ static int read8(const envref *r, int addr) {
     const gbxo_ctx *x = r->x;
     int a16 = addr & 0xFFFF;
     if (a16 >= 0xE000 && a16 < 0xFE00) a16 -= 0x2000;
+    if (x->ram_ops && a16 >= ROM_LIMIT) x->ram_ops[r->i]++;
     const int32_t *cs = x->cart_state + (int64_t)r->i * CS_STRIDE;
     if (a16 < BOOTROM_SIZE && cs[CS_BOOTROM] != 0) return x->bootrom[a16];
     if (a16 < ROM_LIMIT) {
@@ -318,6 +326,7 @@ static void write8(const envref *r, int addr, int val) {
     uint8_t v8 = (uint8_t)val;
     uint8_t *m = x->mem + r->base;
     int32_t *cs = x->cart_state + (int64_t)i * CS_STRIDE;
+    if (x->ram_ops && a16 >= ROM_LIMIT) x->ram_ops[i] += a16 == 0xFF46 ? 321 : 1;
     switch (a16) {
     case 0xFF00: {
         int sel = v8 & 0x30;

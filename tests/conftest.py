@@ -36,4 +36,17 @@ def case_rom(case: dict, micro: dict) -> bytes:
 
     if case["rom"]["kind"] == "config":
         return roms.CONFIG_ROMS[case["rom"]["id"]]()
+    if case["rom"]["kind"] == "isa_probe":
+        from tests import isa_probe
+
+        return isa_probe.rom_image()
     return micro[case["rom"]["id"]]
+
+
+def case_setup_state(case: dict, rom: bytes) -> dict | None:
+    """Per-env start state a golden case writes after reset (None: reset alone)."""
+    if case.get("setup") == "isa_probe":
+        from tests import isa_probe
+
+        return isa_probe.initial_state(rom)
+    return None

@@ -40,6 +40,7 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(HERE))
+sys.path.insert(0, str(REPO / "tests"))
 
 from gbxcule_b200 import roms  # noqa: E402
 from gbxcule_b200 import state as st  # noqa: E402
@@ -56,6 +57,8 @@ MICRO = [  # (name, frames_per_step, release_after_frames) from suite.yaml
 ]
 
 
+LONG_STEPS = 100
+
 # unit 200 of config 1's loop: an instruction start every env reaches in the first step
 TRAP_PC_CONFIG1 = "0x0326"
 
@@ -66,6 +69,29 @@ def _sha(b: bytes) -> str:
 
 def _ref_state(be) -> dict:
     return {k: getattr(be, v).numpy() for k, v in st.REF_ATTR.items()}
+
+
+def _ref_load(be, state: dict) -> None:
+    """Write a state dict (``export_state`` layout) into the reference backend's arrays."""
+    import array
+
+    for name, attr in st.REF_ATTR.items():
+        if name not in state:
+            continue
+        dst = getattr(be, attr).data
+        vals = np.asarray(state[name]).reshape(-1)
+        if isinstance(dst, bytearray):
+            dst[:] = vals.astype(np.uint8).tobytes()
+        else:
+            dst[:] = array.array(dst.typecode, vals.tolist())
+
+
+def _setup(case: dict, be) -> None:
+    """Per-env start state of a case that does not start from reset alone."""
+    if case.get("setup") == "isa_probe":
+        import isa_probe
+
+        _ref_load(be, isa_probe.initial_state(isa_probe.rom_image()))
 
 
 def _actions(kind: str, rng, n: int) -> np.ndarray:
@@ -88,6 +114,10 @@ def run_case(args) -> dict:
     boot = tmp / "boot.bin"
     boot.write_bytes(roms.boot_stub())
     rom_bytes = bytes.fromhex(case.pop("_rom_hex")) if "_rom_hex" in case else None
+    if rom_bytes is None and case["rom"]["kind"] == "isa_probe":
+        import isa_probe
+
+        rom_bytes = isa_probe.rom_image()
     if rom_bytes is None:
         rom_bytes = roms.CONFIG_ROMS[case["rom"]["id"]]()
     rom_path = tmp / "rom.gb"
@@ -120,12 +150,16 @@ def _run_case(ref_root, case, rom_bytes, rom_path, boot) -> dict:
     t0 = time.time()
     be.reset()
     case["reset_digest"] = st.digest(_ref_state(be))
+    _setup(case, be)
+    if "setup" in case:
+        case["setup_digest"] = st.digest(_ref_state(be))
     rng = np.random.default_rng(case["action_seed"])
     steps = []
     render = case.get("render", False)
+    draw = case.get("action_envs", n)  # actions drawn for this many envs; the first n are used
 
     def do_step():
-        act = _actions(case["actions"], rng, n)
+        act = _actions(case["actions"], rng, draw)[:n]
         ref.launch_step(be, act, render=render_bg)
         rec = {"actions": act.tolist(), "digest": st.digest(_ref_state(be))}
         if render_bg:
@@ -206,6 +240,28 @@ def cases(micro: dict) -> list[dict]:
                            ("trap_watch_div", 2, {"GBXCULE_WATCH_ADDR": "0xFF04"})]:  # DIV register
         cs.append(dict(name=name, rom={"kind": "config", "id": cfg}, num_envs=4, frames=24, release=8,
                        stage="obs_only", actions="uniform9", action_seed=30 + cfg, steps=3, env=env))
+    # long horizons: 100 env-steps per config on 2 envs (configs 4 and 5 after the
+    # 600-frame warm-up and a restore of every env from env 0, then seeded
+    # masked restores each step). Config 1 uses the benchmark's own action
+    # stream (default_rng(0) draws for 64 envs per step; envs 0-1 here).
+    cs += [
+        dict(name="config1_long", rom={"kind": "config", "id": 1}, num_envs=2, action_envs=64, frames=24,
+             release=8, stage="obs_only", actions="uniform9", action_seed=0, steps=LONG_STEPS),
+        dict(name="config2_long", rom={"kind": "config", "id": 2}, num_envs=2, frames=24, release=8,
+             stage="obs_only", actions="uniform9", action_seed=12, steps=LONG_STEPS, render=True),
+        dict(name="config3_long", rom={"kind": "config", "id": 3}, num_envs=2, frames=24, release=8,
+             stage="obs_only", actions="bernoulli", action_seed=13, steps=LONG_STEPS),
+        dict(name="config4_long", rom={"kind": "config", "id": 4}, num_envs=2, frames=24, release=8,
+             stage="obs_only", actions="uniform9", action_seed=14, steps=LONG_STEPS, warmup=25,
+             restore={"snapshot_env": 0, "rate": 0.1, "mask_seed": 1104}),
+        dict(name="config5_long", rom={"kind": "config", "id": 5}, num_envs=2, frames=24, release=8,
+             stage="obs_only", actions="uniform9", action_seed=15, steps=LONG_STEPS, warmup=25, render=True,
+             restore={"snapshot_env": 0, "rate": 0.1, "mask_seed": 1105}),
+    ]
+    # every opcode once (conditionals taken and not taken), one env each, then a
+    # trap: lengths, cycles and the trap set against the reference (tests/isa_probe.py)
+    cs.append(dict(name="isa_probe", rom={"kind": "isa_probe"}, setup="isa_probe", num_envs=527, frames=1,
+                   release=1, stage="obs_only", actions="uniform8", action_seed=40, steps=1))
     for name, frames, release in MICRO:
         steps = 3 if frames > 1 else 8
         cs.append(dict(name=f"micro_{name}", rom={"kind": "micro", "id": name}, num_envs=3,

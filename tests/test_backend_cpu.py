@@ -1,7 +1,8 @@
 """Host-side behaviour of the backend that needs no GPU: argument checks made
 when the backend is built, the reference's "not initialized" errors before
 ``reset()`` (src/gbxcule/backends/warp_vec.py:503-901), and an idempotent
-``close()``. Nothing here touches a device: ``reset()`` is never called."""
+``close()``. Nothing here touches a device or loads libgbx: ``reset()`` is
+never called, and the library is loaded by the first ``reset()``."""
 
 from __future__ import annotations
 
@@ -31,7 +32,13 @@ def test_constructor_rejects_bad_arguments(rom, kw, message):
         GbxVecCudaBackend(rom, **kw)
 
 
-def test_calls_before_reset_raise_the_reference_errors(rom):
+def test_calls_before_reset_raise_the_reference_errors(rom, monkeypatch):
+    from gbxcule_b200 import _lib
+
+    def no_library():
+        raise AssertionError("libgbx loaded before reset()")
+
+    monkeypatch.setattr(_lib, "lib", no_library)  # no toolkit needed before reset()
     be = GbxVecCudaBackend(rom, num_envs=2, render_pixels=True, render_pixels_packed=True)
     try:
         for call in (lambda: be.step(np.zeros(2, np.int32)), lambda: be.get_cpu_state(0),

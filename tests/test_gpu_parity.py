@@ -18,7 +18,7 @@ import pytest
 from gbxcule_b200 import roms
 from gbxcule_b200 import state as st
 from oracle import OracleEnvs
-from tests.conftest import case_rom
+from tests.conftest import case_rom, case_setup_state
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -60,6 +60,10 @@ def test_golden_case_on_gpu(case, micro_roms, monkeypatch):
                   render_pixels_packed=True, render_on_step=False, render_bg=case.get("render_bg", False))
     try:
         assert st.digest(be.export_state()) == case["reset_digest"]
+        init = case_setup_state(case, rom)
+        if init is not None:
+            be.import_state(init)
+            assert st.digest(be.export_state()) == case["setup_digest"]
         trace, warm = case["trace"], case.get("warmup", 0)
         for rec in trace[:warm]:
             _step(be, rec["actions"])
@@ -137,6 +141,7 @@ FULL = [  # benchmark-size workloads: (config, envs, steps, action kind, restore
     (2, 4096, 3, "uniform9", 0.0),
     (3, 16384, 2, "bernoulli", 0.0),
     (4, 65536, 2, "uniform9", 0.05),
+    (5, 131072, 3, "uniform9", 0.05),
 ]
 
 
@@ -176,6 +181,27 @@ def test_full_size_sampled_envs_match_oracle(cfg, n, steps, kind, rate):
             torch.cuda.synchronize()
             pix = be.pixels_packed_torch().cpu().numpy()[sample]
             assert np.array_equal(pix, o.render_packed()), f"render step {k}"
+    finally:
+        be.close()
+
+
+def test_config1_benchmark_size_every_step():
+    """Config 1 as specified: 64 envs x 1,000 env-steps, the full state checked
+    after every step against the oracle's committed per-step digests."""
+    import json
+    from tests.conftest import GOLDEN
+
+    tr = json.loads((GOLDEN / "config1_1000.json").read_text())
+    n = tr["envs"]
+    be = _backend(roms.config1_rom(), n, tr["frames"], tr["release"])
+    try:
+        assert st.digest(be.export_state()) == tr["reset_digest"]
+        rng = np.random.default_rng(tr["action_seed"])
+        acts = torch.empty(n, dtype=torch.int32, device="cuda")
+        for k, want in enumerate(tr["digests"]):
+            acts.copy_(torch.from_numpy(roms.uniform_actions(rng, n, 9)))
+            be.step_torch(acts)
+            assert st.digest(be.export_state()) == want, f"step {k}"
     finally:
         be.close()
 
@@ -373,3 +399,35 @@ def test_policy_rollout_with_resets_replays_on_oracle():
         assert not st.diff(be.export_state(), o.state(), n)
     finally:
         be.close()
+
+
+def test_two_rank_slices_equal_one_batch():
+    """Two handles on one GPU, each a rank's contiguous env slice stepped with
+    its own action stream (multi.rank_seed), end in the states one batch of
+    all the global env ids reaches with the same per-slice streams."""
+    from gbxcule_b200 import multi
+
+    rom, per, world, steps = roms.config5_rom(), 192, 2, 3
+    whole = _backend(rom, per * world, 24, 8)
+    parts = [_backend(rom, per, 24, 8) for _ in range(world)]
+    rngs = [np.random.default_rng(multi.rank_seed(11, r)) for r in range(world)]
+    try:
+        for _ in range(steps):
+            acts = [roms.uniform_actions(g, per, 9) for g in rngs]
+            for be, a in zip(parts, acts):
+                _step(be, a)
+            _step(whole, np.concatenate(acts))
+        full = whole.export_state()
+        for r, be in enumerate(parts):
+            lo, hi = multi.rank_env_slice(r, world, per)
+            mine = be.export_state()
+            for name in st.ORDER:
+                if name.startswith("latch_"):  # env-0 latches belong to each batch's env 0
+                    continue
+                a = np.asarray(mine[name]).reshape(per, -1)
+                b = np.asarray(full[name]).reshape(per * world, -1)[lo:hi]
+                assert np.array_equal(a, b), f"rank {r} field {name}"
+    finally:
+        whole.close()
+        for be in parts:
+            be.close()

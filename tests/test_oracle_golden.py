@@ -16,7 +16,7 @@ import pytest
 from gbxcule_b200 import roms
 from gbxcule_b200 import state as st
 from oracle import OracleEnvs
-from tests.conftest import case_rom
+from tests.conftest import case_rom, case_setup_state
 
 
 def _sha(b: bytes) -> str:
@@ -38,6 +38,11 @@ def test_oracle_matches_reference(case, micro_roms, monkeypatch):
         monkeypatch.setenv(k, v)
     o = OracleEnvs(rom, roms.boot_stub(), case["num_envs"], stage=case["stage"])
     assert st.digest(o.state()) == case["reset_digest"]
+    init = case_setup_state(case, rom)
+    if init is not None:
+        for name, arr in init.items():
+            o.s[name][:] = np.asarray(arr).reshape(o.s[name].shape)
+        assert st.digest(o.state()) == case["setup_digest"]
     trace = case["trace"]
     warm = case.get("warmup", 0)
     for rec in trace[:warm]:
