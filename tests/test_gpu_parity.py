@@ -167,8 +167,9 @@ def test_full_size_sampled_envs_match_oracle(cfg, n, steps, kind, rate):
         snap_o = o.snapshot(0)
         for k in range(steps):
             a = _acts(kind, rng, n)
-            _step(be, a)
+            _step(be, a)  # render_on_step: the frames come from the state before the restore
             o.step(a[sample], 24, 8)
+            want_pix = o.render_packed()
             if rate > 0:
                 mask = (np.random.default_rng(2000 + k).random(n) < rate)
                 cache.apply_mask_torch(torch.as_tensor(mask, device="cuda"))
@@ -180,7 +181,7 @@ def test_full_size_sampled_envs_match_oracle(cfg, n, steps, kind, rate):
                 assert np.array_equal(got[name], o.s[name]), f"config {cfg} step {k} field {name}"
             torch.cuda.synchronize()
             pix = be.pixels_packed_torch().cpu().numpy()[sample]
-            assert np.array_equal(pix, o.render_packed()), f"render step {k}"
+            assert np.array_equal(pix, want_pix), f"render step {k}"
     finally:
         be.close()
 
