@@ -13,7 +13,7 @@ import ctypes
 from ctypes import POINTER, c_char_p, c_int32, c_int64, c_size_t, c_uint32, c_void_p
 
 GBX_OK, GBX_ERR_INVALID, GBX_ERR_CUDA, GBX_ERR_OOM, GBX_ERR_STATE, GBX_ERR_RANGE = range(6)
-ABI_VERSION = 3  # include/gbx.h GBX_ABI_VERSION
+ABI_VERSION = 4  # include/gbx.h GBX_ABI_VERSION
 
 BUF = {"mem": 0, "pixels": 1, "pixels_packed": 2, "obs": 3, "reward": 4, "cart_ram": 5,
        "serial": 6, "i32": 7, "i64": 8, "u8": 9, "cart_state": 10, "latch": 11, "frame_bg": 12}
@@ -35,7 +35,12 @@ class Info(ctypes.Structure):
     _fields_ = [("num_envs", c_int32), ("env_stride", c_int32), ("device", c_int32), ("stage", c_int32),
                 ("mbc_kind", c_int32), ("rom_bytes", c_int32), ("rom_bank_count", c_int32),
                 ("rom_bank_mask", c_int32), ("ram_bank_count", c_int32), ("ram_bytes", c_int32),
-                ("sm_count", c_int32), ("envs_per_warp", c_int32), ("envs_per_warp_tuned", c_int32)]
+                ("sm_count", c_int32), ("envs_per_warp", c_int32), ("envs_per_warp_tuned", c_int32),
+                ("dispatch", c_int32)]
+
+
+# gbx_dispatch (include/gbx.h)
+DISPATCH = {"auto": 0, "switch": 1, "uniform": 2}
 
 
 class BufferInfo(ctypes.Structure):
@@ -83,6 +88,7 @@ def lib():
         "gbx_render_bg_env0": ([P, P, P], c_int32),
         "gbx_set_debug_traps": ([P, c_int32, c_int32, c_int64, c_int32], c_int32),
         "gbx_set_envs_per_warp": ([P, c_int32], c_int32),
+        "gbx_set_dispatch": ([P, c_int32], c_int32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -571,6 +571,20 @@ class GbxVecCudaBackend:
         self._need()
         L.check(self._lib.gbx_set_envs_per_warp(self._h, int(k)), "gbx_set_envs_per_warp")
 
+    def dispatch(self) -> str:
+        """Interpreter of the latest step launch: "switch" or "uniform"."""
+        self._need()
+        info = L.Info()
+        L.check(self._lib.gbx_get_info(self._h, ctypes.byref(info)))
+        return "uniform" if info.dispatch == L.DISPATCH["uniform"] else "switch"
+
+    def set_dispatch(self, mode: str) -> None:
+        """Fix the step kernel's interpreter ("switch" or "uniform"), or "auto"."""
+        self._need()
+        if mode not in L.DISPATCH:
+            raise ValueError(f"dispatch must be one of {sorted(L.DISPATCH)}, got {mode!r}")
+        L.check(self._lib.gbx_set_dispatch(self._h, L.DISPATCH[mode]), "gbx_set_dispatch")
+
     def device_status(self, clear: bool = False) -> int:
         """Device error bits (1: an env's mbc_kind differs from the cartridge)."""
         self._need()

@@ -16,9 +16,10 @@
 
 namespace gbx {
 cudaError_t launch_step(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames, int release,
-                        int stage, cudaStream_t stream, const DebugCfg& dbg, int K, int sms);
+                        int stage, cudaStream_t stream, const DebugCfg& dbg, int K, int sms, bool uniform);
 int fill_envs_per_warp(long long n, int sms);
 int envs_per_warp_override();
+int dispatch_override();
 cudaError_t launch_render_bg_env0(const DevState& st, uint8_t* out, cudaStream_t stream);
 void predecode_rom(const uint8_t* rom, int n, uint32_t* out);
 cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
@@ -35,22 +36,28 @@ static_assert((int)GBX_I32_COUNT == (int)I32_COUNT, "i32 field table mismatch");
 static_assert((int)GBX_I64_COUNT == (int)I64_COUNT, "i64 field table mismatch");
 static_assert((int)GBX_U8_COUNT == (int)U8_COUNT, "u8 field table mismatch");
 
-// Envs per warp (K) of the step kernel, chosen per handle. K only changes
-// which lanes run which envs, never a result. Automatic mode times its
-// candidates on the handle's first real steps, in the order A B B A (or
-// A B C C B A) so that a step time drifting as the envs diverge weighs on
-// every candidate alike, and keeps the fastest. Timing uses events around the
-// step launches already requested; no step is added or repeated.
+// Launch shape of the step kernel, chosen per handle: envs per warp K and
+// the interpreter (switch or uniform datapath). Neither changes a result.
+// A shape is coded as K | UNI_BIT. Automatic mode times its candidates on the
+// handle's first real steps, in the order A B B A (A B C C B A, ...) so that
+// a step time drifting as the envs diverge weighs on every candidate alike,
+// and keeps the fastest. Timing uses events around the step launches already
+// requested; no step is added or repeated.
+constexpr int UNI_BIT = 64;
+inline int shape_k(int m) { return m & 63; }
+inline bool shape_uni(int m) { return (m & UNI_BIT) != 0; }
 struct KTuner {
-  static constexpr int MAXC = 3;
+  static constexpr int MAXC = 5;
   int fixed = 0;              // > 0: K set by the caller or GBX_ENVS_PER_WARP
-  int ncand = 0, cand[MAXC] = {0, 0, 0};
-  int order[2 * MAXC] = {0, 0, 0, 0, 0, 0};
+  int disp = 0;               // gbx_dispatch set by the caller or GBX_DISPATCH
+  int ncand = 0, cand[MAXC] = {};
+  int order[2 * MAXC] = {};
   int launched = 0;           // trials launched (events recorded)
   int measured = 0;           // trials whose events were read
-  float ms[MAXC] = {0, 0, 0};
+  float ms[MAXC] = {};
   cudaEvent_t ev[2 * MAXC][2] = {};
-  int best = 0;               // chosen K once every trial is measured
+  int best = 0;               // chosen shape once every trial is measured
+  bool settled() const { return ncand <= 1 || measured == 2 * ncand; }
 };
 
 struct gbx_env {
@@ -66,7 +73,7 @@ struct gbx_env {
   bool initialized;
   int sm_count;            // SMs of the handle's device
   KTuner tune;
-  int last_k;              // K of the latest step launch
+  int last_shape;          // launch shape of the latest step launch (0: none yet)
   // Owners: the creator (dropped by gbx_destroy) plus one per live DLPack
   // tensor (dropped by its deleter). Device memory is freed with the last.
   std::atomic<int> refs;
@@ -165,20 +172,33 @@ void free_env(gbx_env* h) {
       if (e) cudaEventDestroy(e);
 }
 
-// Candidates of the automatic K choice for n envs on `sms` SMs: the K that
-// fills one wave of warps, half of it (two waves of emptier warps) and 32.
-void tuner_init(KTuner& t, int n, int sms, int fixed) {
+// Candidates of the automatic choice for n envs on `sms` SMs. K: the one
+// that fills one wave of warps, half of it (two waves of emptier warps) and
+// 32, or the fixed K. Interpreter: the switch at every candidate K, the
+// uniform datapath at the K that fill warps at least half (with fewer lanes
+// a fixed datapath wastes most of its issue slots), or the fixed one.
+void tuner_init(KTuner& t, int n, int sms, int fixed, int disp) {
   t = KTuner();
   t.fixed = fixed;
+  t.disp = disp;
+  int ks[3] = {0, 0, 0}, nk = 0;
   const int kf = fill_envs_per_warp(n, sms);
-  t.cand[t.ncand++] = kf;
-  if (kf > 1) t.cand[t.ncand++] = kf / 2;
-  if (kf < 32) t.cand[t.ncand++] = 32;
+  if (fixed) ks[nk++] = fixed;
+  else {
+    ks[nk++] = kf;
+    if (kf > 1) ks[nk++] = kf / 2;
+    if (kf < 32) ks[nk++] = 32;
+  }
+  for (int i = 0; i < nk; i++)
+    if (disp != GBX_DISPATCH_UNIFORM && t.ncand < KTuner::MAXC) t.cand[t.ncand++] = ks[i];
+  for (int i = 0; i < nk; i++)
+    if ((disp == GBX_DISPATCH_UNIFORM || (disp == GBX_DISPATCH_AUTO && ks[i] >= 16)) && t.ncand < KTuner::MAXC)
+      t.cand[t.ncand++] = ks[i] | UNI_BIT;
   for (int i = 0; i < t.ncand; i++) {
     t.order[i] = i;
     t.order[2 * t.ncand - 1 - i] = i;
   }
-  t.best = kf;
+  t.best = t.cand[0];
 }
 
 // Read the events of finished trials; once all are read, keep the fastest K.
@@ -191,7 +211,7 @@ void tuner_poll(KTuner& t) {
     t.ms[t.order[t.measured]] += ms;
     t.measured++;
   }
-  if (t.measured == 2 * t.ncand) {
+  if (t.ncand > 1 && t.measured == 2 * t.ncand) {
     int b = 0;
     for (int i = 1; i < t.ncand; i++)
       if (t.ms[i] < t.ms[b]) b = i;
@@ -357,7 +377,7 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
     return fail(GBX_ERR_CUDA, "cannot read the SM count of device %d", cfg->device);
   }
   h->sm_count = sms;
-  tuner_init(h->tune, st.n, sms, envs_per_warp_override());
+  tuner_init(h->tune, st.n, sms, envs_per_warp_override(), dispatch_override());
   *out = h;
   return GBX_OK;
 }
@@ -382,9 +402,11 @@ int gbx_get_info(const gbx_env* h, gbx_info* out) {
   out->ram_bank_count = h->st.ram_bank_count;
   out->ram_bytes = h->ram_bytes;
   out->sm_count = h->sm_count;
-  if (!h->tune.fixed) tuner_poll(const_cast<gbx_env*>(h)->tune);  // trials that have finished since
-  out->envs_per_warp = h->tune.fixed ? h->tune.fixed : h->last_k ? h->last_k : h->tune.best;
-  out->envs_per_warp_tuned = h->tune.fixed ? 1 : h->tune.measured == 2 * h->tune.ncand;
+  tuner_poll(const_cast<gbx_env*>(h)->tune);  // trials that have finished since
+  const int shape = h->last_shape ? h->last_shape : h->tune.best;
+  out->envs_per_warp = shape_k(shape);
+  out->envs_per_warp_tuned = h->tune.settled();
+  out->dispatch = shape_uni(shape) ? GBX_DISPATCH_UNIFORM : GBX_DISPATCH_SWITCH;
   return GBX_OK;
 }
 
@@ -397,8 +419,9 @@ int gbx_reset(gbx_env* h, void* stream) {
   h->initialized = true;
   if (h->cfg.stage == STAGE_OBS || h->cfg.stage == STAGE_FULL) {
     const int32_t* zero_actions = h->st.i32 + (size_t)F_ACTIONS * h->st.S;
-    const int K = h->tune.fixed ? h->tune.fixed : h->tune.best;
-    CK(launch_step(h->st, h->pre, zero_actions, 0, 0, h->cfg.stage, s, h->dbg, K, h->sm_count),
+    const int shape = h->tune.best;
+    CK(launch_step(h->st, h->pre, zero_actions, 0, 0, h->cfg.stage, s, h->dbg, shape_k(shape), h->sm_count,
+                   shape_uni(shape)),
        "step kernel (reset obs)");
   }
   return GBX_OK;
@@ -412,24 +435,22 @@ int gbx_step(gbx_env* h, const int32_t* actions, int32_t frames, int32_t release
   DeviceGuard g(h->cfg.device);
   cudaStream_t s = S_(stream);
   KTuner& t = h->tune;
-  int K = t.fixed;
   cudaEvent_t* trial = nullptr;
-  if (!K) {
-    tuner_poll(t);
-    K = t.best;
-    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    // trials only on real steps, outside stream capture and debug traps
-    if (t.launched < 2 * t.ncand && frames > 0 && !h->dbg.active() &&
-        cudaStreamIsCapturing(s, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone) {
-      trial = t.ev[t.launched];
-      for (int k = 0; k < 2; k++)
-        if (!trial[k]) CK(cudaEventCreate(&trial[k]), "tuner event");
-      K = t.cand[t.order[t.launched]];
-      CK(cudaEventRecord(trial[0], s), "tuner event record");
-    }
+  tuner_poll(t);
+  int shape = t.best;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  // trials only on real steps, outside stream capture and debug traps
+  if (t.ncand > 1 && t.launched < 2 * t.ncand && frames > 0 && !h->dbg.active() &&
+      cudaStreamIsCapturing(s, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusNone) {
+    trial = t.ev[t.launched];
+    for (int k = 0; k < 2; k++)
+      if (!trial[k]) CK(cudaEventCreate(&trial[k]), "tuner event");
+    shape = t.cand[t.order[t.launched]];
+    CK(cudaEventRecord(trial[0], s), "tuner event record");
   }
-  h->last_k = K;
-  CK(launch_step(h->st, h->pre, actions, frames, release, h->cfg.stage, s, h->dbg, K, h->sm_count),
+  h->last_shape = shape;
+  CK(launch_step(h->st, h->pre, actions, frames, release, h->cfg.stage, s, h->dbg, shape_k(shape),
+                 h->sm_count, shape_uni(shape)),
      "step kernel");
   if (trial) {
     CK(cudaEventRecord(trial[1], s), "tuner event record");
@@ -438,16 +459,30 @@ int gbx_step(gbx_env* h, const int32_t* actions, int32_t frames, int32_t release
   return GBX_OK;
 }
 
-int gbx_set_envs_per_warp(gbx_env* h, int32_t k) {
-  RET(check_env(h));
-  if (k < 0 || k > 32) return fail(GBX_ERR_INVALID, "envs_per_warp must be in [0, 32], got %d", k);
+// New tuner state for a fixed K (0 = automatic) and dispatch (0 = automatic).
+static void retune(gbx_env* h, int k, int disp) {
   DeviceGuard g(h->cfg.device);
   cudaDeviceSynchronize();  // no trial of the previous setting is still in flight
   KTuner fresh;
-  tuner_init(fresh, h->st.n, h->sm_count, k);
+  tuner_init(fresh, h->st.n, h->sm_count, k, disp);
   for (int i = 0; i < 2 * KTuner::MAXC; i++)  // keep the created events
     for (int j = 0; j < 2; j++) fresh.ev[i][j] = h->tune.ev[i][j];
   h->tune = fresh;
+  h->last_shape = 0;
+}
+
+int gbx_set_envs_per_warp(gbx_env* h, int32_t k) {
+  RET(check_env(h));
+  if (k < 0 || k > 32) return fail(GBX_ERR_INVALID, "envs_per_warp must be in [0, 32], got %d", k);
+  retune(h, k, h->tune.disp);
+  return GBX_OK;
+}
+
+int gbx_set_dispatch(gbx_env* h, int32_t d) {
+  RET(check_env(h));
+  if (d < GBX_DISPATCH_AUTO || d > GBX_DISPATCH_UNIFORM)
+    return fail(GBX_ERR_INVALID, "dispatch must be 0 (auto), 1 (switch) or 2 (uniform), got %d", d);
+  retune(h, h->tune.fixed, d);
   return GBX_OK;
 }
 

@@ -45,8 +45,10 @@
 #include <limits.h>
 #include <stdint.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include "gbx_layout.h"
+#include "gbx_udesc.h"
 
 namespace gbx {
 
@@ -126,6 +128,8 @@ __host__ __device__ constexpr DecodeTable make_table() {
   return t;
 }
 __constant__ DecodeTable c_decode = make_table();
+// descriptors of the uniform interpreter (gbx_udesc.h), staged in shared memory
+__constant__ UDescTable c_udesc = make_udesc_table();
 
 // Host: pre-decode a ROM image (every byte offset as an instruction start).
 void predecode_rom(const uint8_t* rom, int n, uint32_t* out) {
@@ -225,6 +229,21 @@ struct Hot {
       default: r = a | v; f = (r == 0) << 7; break;
     }
     setA(r);
+  }
+  // DAA (alu.py)
+  __device__ __forceinline__ void daa() {
+    int a = A(), n = (f >> 6) & 1, hf = (f >> 5) & 1, c = (f >> 4) & 1, adj = 0, carry = c;
+    if (!n) {
+      if (hf || (a & 0xF) > 9) adj |= 0x06;
+      if (c || a > 0x99) { adj |= 0x60; carry = 1; }
+      a = (a + adj) & 0xFF;
+    } else {
+      if (hf) adj |= 0x06;
+      if (c) adj |= 0x60;
+      a = (a - adj) & 0xFF;
+    }
+    f = FLAGS(a == 0, n, 0, carry);
+    setA(a);
   }
   __device__ __forceinline__ bool cond(int cc) const {
     int bit = (cc & 2) ? ((f >> 4) & 1) : ((f >> 7) & 1);
@@ -960,6 +979,191 @@ struct Emu {
 __device__ __forceinline__ int sign8(int v) { return v >= 128 ? v - 256 : v; }
 
 // ---------------------------------------------------------------------------
+// Uniform-datapath interpreter loop (gbx_udesc.h)
+// ---------------------------------------------------------------------------
+// Every lane runs the same stages for its own instruction: fetch, descriptor,
+// operands, effective address, reads, adder / logic / rotate units, register,
+// flag and memory results, PC, SP and cycles. Divergence is left to the
+// memory accesses that miss the inline fast path (IO, cartridge registers,
+// fetches outside the staged words), the special opcodes and the exact
+// post-instruction tail, as in the switch loop. Same results, instruction for
+// instruction, as the switch loop (both follow the reference templates).
+template <int MBC>
+__device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int& ninstr, int& win_hi,
+                                             int& bankN_off, int& cram_off, const uint32_t* pre_s,
+                                             const uint32_t* __restrict__ pre_g, int pre_s_words,
+                                             const uint8_t* dec_s, const uint4* ud_s, int frames_to_run) {
+  uint8_t* const mem = s.mem;
+  uint8_t* const cram = s.cart_ram;
+  // byte reads and writes: VRAM, WRAM, HRAM and the mapped cart-RAM bank as
+  // one predicated access; JOYP inline; the rest out of line
+  auto urd = [&](int a) -> int {
+    const bool pl = ((a >> 13) | 2) == 6 || (unsigned)(a - 0xFF80) < 0x7Fu;
+    const bool cr = (unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0;
+    const uint8_t* p = pl ? mem + a : cram + (cram_off + a - 0xA000);
+    if (pl || cr) return *p;
+    if (a == 0xFF00) return s.joyp;
+    s.clk = h.clk;
+    return s.read_slow(a);
+  };
+  auto uwr = [&](int a, int v) {
+    const bool pl = ((a >> 13) | 2) == 6 || (unsigned)(a - 0xFF80) < 0x7Fu;
+    const bool cr = (unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0;
+    uint8_t* p = pl ? mem + a : cram + (cram_off + a - 0xA000);
+    if (pl || cr) { *p = (uint8_t)v; return; }
+    if (a == 0xFF00) { s.write_joyp(v); return; }
+    s.clk = h.clk;
+    s.write_slow(a, v);
+    h.clk = s.clk;
+    if (s.ev) h.next_ev = INT_MIN;
+    win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
+  };
+
+  while (run) {
+    const int pc = h.pc;
+    // ---- fetch: staged words, the switched bank's words, or out of line ----
+    uint32_t w;
+    {
+      const bool ins = (unsigned)pc < (unsigned)win_hi;
+      const bool inn = (unsigned)(pc - 0x4000) < 0x3FFEu && bankN_off >= 0;
+      const int idx = ins ? pc : pc + bankN_off;
+      if (ins || (inn && idx < pre_s_words)) w = pre_s[idx];
+      else if (inn) w = __ldg(pre_g + idx);
+      else { s.clk = h.clk; w = s.fetch_slow(pc, dec_s); }
+    }
+    const int op = w & 0xFF, b1 = (w >> 8) & 0xFF, imm16 = (w >> 8) & 0xFFFF;
+    const int key = op == 0xCB ? 256 + b1 : op;
+    const uint4 q0 = ud_s[2 * key], q1 = ud_s[2 * key + 1];
+    const uint32_t fa = q0.z, vx = q1.x, vy = q1.y;
+    const int F = h.f;
+    const bool taken = ((F ^ (int)(vy >> 8)) & (int)vy & 0xFF) == 0;
+    // ---- operands and effective address ----
+    const int A = h.A();
+    const int xr = __byte_perm(h.bcde, h.hlxa, q0.x);
+    const int pr = __byte_perm(h.bcde, h.hlxa, q0.x >> 16);
+    const int p16 = (fa & UF_P_SP) ? h.sp : (pr | ((fa & UF_P_AF) ? F : 0));
+    int ea = (fa & UF_EA_SP) ? h.sp : (int)__byte_perm(h.bcde, h.hlxa, q0.y);
+    ea |= (fa & UF_EA_IMM16) ? imm16 : (fa & UF_EA_IMM8) ? b1 : 0;
+    if (fa & UF_EA_FF) ea |= 0xFF00;
+    ea = (ea - (int)((fa >> UF_EA_DEC_BIT) & 1)) & 0xFFFF;
+    // ---- reads (the stack only when a conditional return is taken) ----
+    int v0 = 0, v1 = 0;
+    if ((fa & UF_RD1) && taken) v0 = urd(ea);
+    if ((fa & UF_RD2) && taken) v1 = urd((ea + 1) & 0xFFFF);
+    const int x = (fa & UF_X_MEM) ? v0 : (fa & UF_X_IMM) ? b1 : xr;
+    // ---- adder: 8-bit ALU, INC/DEC, 16-bit pair arithmetic ----
+    const int k16 = (int)(q0.y >> 16);
+    const int e8 = (b1 ^ 0x80) - 0x80;
+    const int lsel = (vx >> UV_LSEL) & 3, rsel = (vx >> UV_RSEL) & 3;
+    const int L = lsel == ULS_A ? A : lsel == ULS_X ? x : lsel == ULS_EA ? ea : p16;
+    const int R = rsel == URS_X ? x : rsel == URS_K ? k16 : rsel == URS_P16 ? p16 : (e8 & 0xFFFF);
+    const int sub = (fa >> UF_SUB_BIT) & 1;
+    const int Rv = R ^ (sub ? 0xFF : 0);
+    const int cin = (((fa & UF_CIN) ? (F >> 4) : 0) & 1) ^ sub;
+    const int S = L + Rv + cin;
+    const int cv = L ^ Rv ^ S;  // carries into each bit
+    const bool wide = fa & UF_WIDE;
+    const int ah = ((cv >> (wide ? 12 : 4)) & 1) ^ sub;
+    const int ac = ((cv >> (wide ? 16 : 8)) & 1) ^ sub;
+    // ---- logic: AND / OR / XOR (also BIT, RES, SET, CPL) ----
+    const int P = (fa & UF_LX) ? x : A;
+    const int Q = (fa & UF_QK) ? k16 : x;
+    const int lop = (vx >> UV_LOP) & 3;
+    const int la = P & Q, lo = P | Q;
+    const int lres = lop == UL_AND ? la : lop == UL_OR ? lo : (lo ^ la);
+    // ---- rotate / shift / swap ----
+    const int cf = (F >> 4) & 1;
+    const int z3 = (x & 1) | (cf << 1) | ((x >> 7) << 2);  // bit0, carry, bit7, 0
+    const int inb = (z3 >> ((vx >> UV_RIN) & 3)) & 1;
+    const bool left = fa & UF_ROT_LEFT;
+    int rres = left ? (((x << 1) | inb) & 0xFF) : ((x >> 1) | (inb << 7));
+    if (fa & UF_SWAP) rres = ((x << 4) | (x >> 4)) & 0xFF;
+    const int rc = left ? (x >> 7) : (x & 1);
+    // ---- 8-bit result and flags ----
+    const int unit = (vx >> UV_UNIT) & 3;
+    const int r8 = unit == UU_PASS ? x : unit == UU_ADD ? (S & 0xFF) : unit == UU_LOGIC ? lres : rres;
+    const int hc = unit == UU_ADD ? ((ah << 5) | (ac << 4)) : unit == UU_ROT ? (rc << 4) : 0;
+    const int fc = ((r8 == 0) << 7) | (sub << 6) | hc;
+    const uint32_t fm = q0.w;  // keep | computed << 8 | set << 16 | xor << 24
+    int Fn = (int)(((((uint32_t)F & fm) | ((uint32_t)fc & (fm >> 8)) | (fm >> 16)) ^ (fm >> 24)) & 0xF0);
+    // ---- memory results (before the registers change: values and addresses
+    //      come from the instruction's inputs) ----
+    const int len = vx & 3;
+    const int seq = pc + len;
+    const int nw = (vx >> UV_NW) & 3;
+    if (nw && taken) {
+      int w0 = r8, a1 = 0, w1 = 0;
+      if (nw == 2) {
+        const int vs = (vy >> UY_VSRC) & 3;
+        const int val = vs == UVS_P16 ? p16 : vs == UVS_PCN ? (seq & 0xFFFF) : h.sp;
+        const bool lof = fa & UF_LOFIRST;
+        w0 = lof ? (val & 0xFF) : (val >> 8);
+        w1 = lof ? (val >> 8) : (val & 0xFF);
+        a1 = (ea + (lof ? 1 : -1)) & 0xFFFF;
+      }
+      uwr(ea, w0);
+      if (nw == 2) uwr(a1, w1);
+    }
+    // ---- register results ----
+    if (fa & UF_D8) {
+      const int pos = (vx >> UV_D8POS) & 31;
+      if (fa & UF_D8_HI) h.hlxa = Hot::insert_byte(h.hlxa, r8, pos);
+      else h.bcde = Hot::insert_byte(h.bcde, r8, pos);
+    }
+    const int spd = (vy >> UY_SPD) & 3;  // 1: SP -= 2, 2: SP += 2
+    if (spd && taken) h.sp = (h.sp + (spd == 1 ? -2 : 2)) & 0xFFFF;
+    const int d16 = (vy >> UY_D16) & 7;
+    if (d16) {
+      const int r16 = (fa & UF_R16_POP) ? (v0 | (v1 << 8)) : (S & 0xFFFF);
+      if (d16 == UD_SP) h.sp = r16;
+      else if (d16 == UD_AF) { h.setA(r16 >> 8); Fn = r16 & 0xF0; }
+      else if (d16 == UD_HL) h.hlxa = (h.hlxa & 0xFFFFu) | ((uint32_t)r16 << 16);
+      else if (d16 == UD_BC) h.bcde = (h.bcde & 0xFFFFu) | ((uint32_t)r16 << 16);
+      else h.bcde = (h.bcde & 0xFFFF0000u) | (uint32_t)r16;
+    }
+    h.f = Fn;
+    // ---- next PC and cycles ----
+    const int tsel = (vx >> UV_TSEL) & 7;
+    int npc = seq;
+    if (taken && tsel)
+      npc = tsel == UT_IMM16 ? imm16 : tsel == UT_JR ? pc + 2 + e8 : tsel == UT_EA ? ea
+          : tsel == UT_V16 ? (v0 | (v1 << 8)) : k16;
+    int cyc = (int)((taken ? (vx >> UV_CYC_T) : (vx >> UV_CYC_NT)) & 15) << 2;
+    // ---- special opcodes (misc.py, stack.py RETI, alu.py DAA) ----
+    if (fa & UF_SPECIAL) {
+      switch (op) {
+        case 0x76: s.halted = 1; s.ev |= EV_HALT; h.next_ev = INT_MIN; break;
+        case 0xF3: s.ime_delay = 0; s.ime = 0; break;
+        case 0xFB: case 0xD9:  // EI, and RETI after its return
+          s.ime_delay = 0;
+          if (!s.ime) { s.ime = 1; s.ev |= EV_IRQ; h.next_ev = INT_MIN; }
+          break;
+        case 0x27: h.daa(); break;
+        default:  // STOP and the unimplemented opcodes (misc.py:42-56)
+          s.trap_op(pc, op, 1);
+          h.next_ev = INT_MIN;
+          npc = pc;
+          cyc = 0;
+          break;
+      }
+    }
+    h.pc = npc & 0xFFFF;
+    // ---- tail ----
+    ninstr++;
+    h.clk += cyc;
+    if (h.clk >= h.next_ev) {
+      if (s.trap) { ninstr--; break; }
+      s.bcde = h.bcde; s.hlxa = h.hlxa; s.f = h.f; s.pc = h.pc; s.sp = h.sp; s.clk = h.clk;
+      const bool done = s.tail_slow(cyc, op, pc, frames_to_run);
+      h.bcde = s.bcde; h.hlxa = s.hlxa; h.f = s.f; h.pc = s.pc; h.sp = s.sp; h.clk = s.clk;
+      h.next_ev = s.next_ev;
+      win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
+      if (done) break;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
 // K = envs per warp: lane l < K of global warp w runs env w*K + l. Small K
@@ -967,7 +1171,14 @@ __device__ __forceinline__ int sign8(int v) { return v >= 128 ? v - 256 : v; }
 // K = 32 packs a full warp (shared issue slots when envs run in lockstep).
 // MAXT = largest block size the launch may use (caps registers at 64K/MAXT).
 // DBG = the debug-trap instantiation (launched only when a trap is set).
-template <int MBC, int MAXT, bool DBG>
+// UNI = the uniform-datapath interpreter (gbx_udesc.h) in place of the
+// per-family switch: for full warps of envs at different PCs.
+// Shared memory: pre-decoded ROM words | boot ROM | family table | (UNI)
+// descriptor table at the next 16-byte boundary.
+__host__ __device__ constexpr size_t udesc_smem_offset(int pre_s_words) {
+  return ((size_t)pre_s_words * 4 + 512 + 15) & ~(size_t)15;
+}
+template <int MBC, int MAXT, bool DBG, bool UNI>
 __global__ void __launch_bounds__(MAXT, 1)
     gb_step_kernel(DevState st, const uint32_t* __restrict__ pre_g, const int32_t* __restrict__ actions,
                    int frames_to_run, int release_after_frames, int stage, int K, int pre_s_words,
@@ -976,6 +1187,7 @@ __global__ void __launch_bounds__(MAXT, 1)
   uint32_t* pre_s = reinterpret_cast<uint32_t*>(smem);
   uint8_t* boot_s = smem + (size_t)pre_s_words * 4;
   uint8_t* dec_s = boot_s + 256;
+  uint4* ud_s = reinterpret_cast<uint4*>(smem + udesc_smem_offset(pre_s_words));
   {
     const uint4* src = reinterpret_cast<const uint4*>(pre_g);
     uint4* dst = reinterpret_cast<uint4*>(pre_s);
@@ -983,6 +1195,10 @@ __global__ void __launch_bounds__(MAXT, 1)
     for (int k = threadIdx.x; k < 256; k += blockDim.x) {
       boot_s[k] = st.boot[k];
       dec_s[k] = c_decode.e[k];
+    }
+    if (UNI) {
+      const uint4* ud = reinterpret_cast<const uint4*>(c_udesc.d);
+      for (int k = threadIdx.x; k < UDESC_KEYS * 2; k += blockDim.x) ud_s[k] = ud[k];
     }
   }
   __syncthreads();
@@ -1118,7 +1334,10 @@ __global__ void __launch_bounds__(MAXT, 1)
     win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
   };
 
-  while (run) {
+  if constexpr (UNI) {
+    uniform_loop<MBC>(s, h, run, ninstr, win_hi, bankN_off, cram_off, pre_s, pre_g, pre_s_words, dec_s, ud_s,
+                      frames_to_run);
+  } else while (run) {
     // ---- fetch + decode ----
     const int pc = h.pc;
     uint32_t w;
@@ -1221,20 +1440,7 @@ __global__ void __launch_bounds__(MAXT, 1)
         cyc = t ? 12 : 8;
         break;
       }
-      case FM_DAA: {
-        int a = h.A(), n = (h.f >> 6) & 1, hf = (h.f >> 5) & 1, c = (h.f >> 4) & 1, adj = 0, carry = c;
-        if (!n) {
-          if (hf || (a & 0xF) > 9) adj |= 0x06;
-          if (c || a > 0x99) { adj |= 0x60; carry = 1; }
-          a = (a + adj) & 0xFF;
-        } else {
-          if (hf) adj |= 0x06;
-          if (c) adj |= 0x60;
-          a = (a - adj) & 0xFF;
-        }
-        h.f = FLAGS(a == 0, n, 0, carry); h.setA(a);
-        break;
-      }
+      case FM_DAA: h.daa(); break;
       case FM_FLAGOP: {  // CPL (YF=5), SCF (YF=6), CCF (YF=7)
         const int zf = (h.f >> 7) & 1, cf = (h.f >> 4) & 1;
         if (YF == 5) { h.setA(h.A() ^ 0xFF); h.f = FLAGS(zf, 1, 1, cf); }
@@ -1530,22 +1736,32 @@ int envs_per_warp_override() {
   return k <= 0 ? 0 : k > 32 ? 32 : k;
 }
 
-template <int MBC, int MAXT, bool DBG>
+// GBX_DISPATCH=switch or =uniform fixes the interpreter for every handle
+// (gbx_dispatch values 1 and 2); unset or anything else = automatic.
+int dispatch_override() {
+  const char* v = getenv("GBX_DISPATCH");
+  if (!v) return 0;
+  if (!strcmp(v, "switch")) return 1;
+  if (!strcmp(v, "uniform")) return 2;
+  return 0;
+}
+
+template <int MBC, int MAXT, bool DBG, bool UNI = false>
 static cudaError_t launch_t(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames,
                             int release, int stage, cudaStream_t stream, int K, int threads, int blocks,
                             int pre_s_words, size_t sm, const DebugCfg& dbg) {
-  cudaError_t e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT, DBG>,
+  cudaError_t e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT, DBG, UNI>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
-  gb_step_kernel<MBC, MAXT, DBG><<<blocks, threads, sm, stream>>>(st, pre, actions, frames, release, stage, K,
-                                                                 pre_s_words, dbg);
+  gb_step_kernel<MBC, MAXT, DBG, UNI><<<blocks, threads, sm, stream>>>(st, pre, actions, frames, release, stage,
+                                                                      K, pre_s_words, dbg);
   return cudaGetLastError();
 }
 
 template <int MBC>
 static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames,
                               int release, int stage, cudaStream_t stream, const DebugCfg& dbg, int K,
-                              int sms) {
+                              int sms, bool uniform) {
   K = K < 1 ? 1 : K > 32 ? 32 : K;
   sms = sms < 1 ? 1 : sms;
   const long long warps = (st.n + K - 1) / K;
@@ -1561,6 +1777,10 @@ static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int
   if (dbg.active())  // debug traps: one instantiation (its 64-register bound fits every block size)
     return launch_t<MBC, 1024, true>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
                                      rom_words, sm, dbg);
+  if (uniform)  // one instantiation: the 64-register bound fits every block size
+    return launch_t<MBC, 1024, false, true>(st, pre, actions, frames, release, stage, stream, K, threads,
+                                            blocks, rom_words,
+                                            udesc_smem_offset(rom_words) + sizeof(UDescTable), dbg);
   if (threads <= 256)
     return launch_t<MBC, 256, false>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
                                      rom_words, sm, dbg);
@@ -1571,13 +1791,18 @@ static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int
                                     rom_words, sm, dbg);
 }
 
-// K = envs per warp (1..32), sms = the device's SM count.
+// K = envs per warp (1..32), sms = the device's SM count, uniform = the
+// uniform-datapath interpreter instead of the switch (ignored while debug
+// traps are set).
 cudaError_t launch_step(const DevState& st, const uint32_t* pre, const int32_t* actions, int frames, int release,
-                        int stage, cudaStream_t stream, const DebugCfg& dbg, int K, int sms) {
+                        int stage, cudaStream_t stream, const DebugCfg& dbg, int K, int sms, bool uniform) {
   switch (st.mbc_kind) {
-    case MBC_MBC1: return launch_mbc<MBC_MBC1>(st, pre, actions, frames, release, stage, stream, dbg, K, sms);
-    case MBC_MBC3: return launch_mbc<MBC_MBC3>(st, pre, actions, frames, release, stage, stream, dbg, K, sms);
-    default: return launch_mbc<MBC_ROM_ONLY>(st, pre, actions, frames, release, stage, stream, dbg, K, sms);
+    case MBC_MBC1:
+      return launch_mbc<MBC_MBC1>(st, pre, actions, frames, release, stage, stream, dbg, K, sms, uniform);
+    case MBC_MBC3:
+      return launch_mbc<MBC_MBC3>(st, pre, actions, frames, release, stage, stream, dbg, K, sms, uniform);
+    default:
+      return launch_mbc<MBC_ROM_ONLY>(st, pre, actions, frames, release, stage, stream, dbg, K, sms, uniform);
   }
 }
 

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define GBX_ABI_VERSION 3
+#define GBX_ABI_VERSION 4
 
 typedef enum {
   GBX_OK = 0,
@@ -88,8 +88,12 @@ typedef struct {
   int32_t rom_bytes, rom_bank_count, rom_bank_mask, ram_bank_count, ram_bytes;
   int32_t sm_count;              /* SMs of the device */
   int32_t envs_per_warp;         /* K of the latest step launch (see gbx_set_envs_per_warp) */
-  int32_t envs_per_warp_tuned;   /* 1 once K is fixed or the automatic choice is made */
+  int32_t envs_per_warp_tuned;   /* 1 once the launch shape is fixed or the automatic choice is made */
+  int32_t dispatch;              /* interpreter of the latest step launch: GBX_DISPATCH_SWITCH or _UNIFORM */
 } gbx_info;
+
+/* Step-kernel interpreters (gbx_set_dispatch). */
+typedef enum { GBX_DISPATCH_AUTO = 0, GBX_DISPATCH_SWITCH = 1, GBX_DISPATCH_UNIFORM = 2 } gbx_dispatch;
 
 typedef struct {
   void* data;                    /* device pointer */
@@ -160,6 +164,18 @@ int gbx_step(gbx_env* env, const int32_t* actions, int32_t frames_to_run,
  * the caller requested, and later steps use the fastest. Synchronises the
  * device. */
 int gbx_set_envs_per_warp(gbx_env* env, int32_t envs_per_warp);
+
+/* Interpreter of the step kernel: GBX_DISPATCH_SWITCH (one switch case per
+ * instruction family; fastest when a warp's envs share their PCs or a warp
+ * holds few envs), GBX_DISPATCH_UNIFORM (every lane runs one fixed datapath
+ * steered by a per-opcode descriptor; fastest for full warps of envs at
+ * different PCs) or GBX_DISPATCH_AUTO (the default: the automatic mode of
+ * gbx_set_envs_per_warp times both among its candidates; GBX_DISPATCH=switch
+ * or =uniform in the environment fixes it for every handle). No counterpart
+ * in the reference, whose cpu_step kernel is one if-chain dispatch
+ * (src/gbxcule/kernels/cpu_step_builder.py:92-125). Never changes a result,
+ * only speed. Synchronises the device. */
+int gbx_set_dispatch(gbx_env* env, int32_t dispatch);
 
 /* Snapshot renderer (ppu_render_downsampled.py:207-234 packed, :182-204 unpacked)
  * from current memory. out: device buffer of at least base_offset + n*1440 bytes

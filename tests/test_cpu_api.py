@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     assert len(names) >= 20
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.gbx_abi_version() == L.ABI_VERSION == 3
+    assert lib.gbx_abi_version() == L.ABI_VERSION == 4
 
 
 def test_create_validates_before_touching_a_device():
@@ -56,6 +56,7 @@ def test_null_handles_are_rejected():
     assert lib.gbx_destroy(None) == L.GBX_OK
     assert lib.gbx_snapshot_destroy(None) == L.GBX_OK
     assert lib.gbx_set_envs_per_warp(None, 4) == L.GBX_ERR_INVALID
+    assert lib.gbx_set_dispatch(None, 2) == L.GBX_ERR_INVALID
 
 
 def test_generators_are_deterministic_with_valid_headers():

@@ -82,22 +82,23 @@ def test_reset_cache_refused_after_reset():
 def test_envs_per_warp_changes_no_result(cfg, n):
     rom = roms.CONFIG_ROMS[cfg]()
     digests = {}
-    for k in (1, 4, 32, 0):
+    for k, disp in ((1, "switch"), (4, "switch"), (32, "switch"), (32, "uniform"), (4, "uniform"), (0, "auto")):
         be = _backend(rom, n, render_pixels_packed=True)
         try:
             be.set_envs_per_warp(k)
+            be.set_dispatch(disp)
             rng = np.random.default_rng(40 + cfg)
             for _ in range(7):
                 _step(be, roms.bernoulli_actions(rng, n) if cfg == 3 else roms.uniform_actions(rng, n))
             be.render_pixels_snapshot_torch()
             torch.cuda.synchronize()
             pix = be.pixels_packed_torch().cpu().numpy().tobytes()
-            digests[k] = (st.digest(be.export_state()), hashlib.sha256(pix).hexdigest())
+            digests[(k, disp)] = (st.digest(be.export_state()), hashlib.sha256(pix).hexdigest())
             used, settled = be.envs_per_warp()
             if k:
-                assert used == k and settled
-            else:  # automatic: 4 or 6 trial steps, then the fastest candidate
-                assert settled and used in (1, 2, 4, 8, 16, 32)
+                assert used == k and settled and be.dispatch() == disp
+            else:  # automatic: 6 trial steps (switch at K = 1 and 32, uniform at 32), then the fastest
+                assert settled and used in (1, 32)
         finally:
             be.close()
     assert len(set(digests.values())) == 1, digests

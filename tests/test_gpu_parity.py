@@ -105,10 +105,15 @@ def _acts(kind, rng, n):
     return roms.bernoulli_actions(rng, n) if kind == "bernoulli" else roms.uniform_actions(rng, n, 9)
 
 
+# automatic mode runs its trial shapes (switch and uniform interpreters) on
+# the first steps; the fixed shape holds the uniform interpreter throughout
+@pytest.mark.parametrize("k,dispatch", [(0, "auto"), (32, "uniform")])
 @pytest.mark.parametrize("cfg,n,steps,frames,release,kind", CONFIG_RUNS)
-def test_cuda_matches_oracle(cfg, n, steps, frames, release, kind):
+def test_cuda_matches_oracle(cfg, n, steps, frames, release, kind, k, dispatch):
     rom = roms.CONFIG_ROMS[cfg]()
     be = _backend(rom, n, frames, release, render_pixels_packed=True, render_on_step=True)
+    be.set_envs_per_warp(k)
+    be.set_dispatch(dispatch)
     o = OracleEnvs(rom, roms.boot_stub(), n)
     rng = np.random.default_rng(100 + cfg)
     try:
