@@ -331,7 +331,9 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
   const size_t S = st.S, n = st.n;
   int rc = GBX_OK;
   uint8_t *rom_d = nullptr, *boot_d = nullptr;
-  if ((rc = dalloc(&rom_d, (size_t)rom_bytes)) || (rc = dalloc(&boot_d, 256)) ||
+  // the ROM is padded with 16 zero bytes: the uniform interpreter fetches an
+  // instruction as the two aligned words around it
+  if ((rc = dalloc(&rom_d, (size_t)rom_bytes + 16)) || (rc = dalloc(&boot_d, 256)) ||
       (rc = dalloc(&st.mem, (size_t)MEM_SIZE * n)) || (rc = dalloc(&st.cart_ram, (size_t)h->ram_rows * n)) ||
       (rc = dalloc(&st.serial, (size_t)SERIAL_MAX * n)) || (rc = dalloc(&st.cart_state, (size_t)CS_STRIDE * S)) ||
       (rc = dalloc(&st.i32, (size_t)I32_COUNT * S)) || (rc = dalloc(&st.i64, (size_t)I64_COUNT * S)) ||
@@ -362,6 +364,7 @@ int gbx_create(const gbx_config* cfg, const uint8_t* rom, size_t rom_len, const 
   }
   predecode_rom(rom, rom_bytes, pre_host);
   cudaError_t e = cudaMemcpy(rom_d, rom, (size_t)rom_bytes, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemset(rom_d + rom_bytes, 0, 16);
   if (e == cudaSuccess) e = cudaMemcpy(boot_d, boot, 256, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(h->pre, pre_host, sizeof(uint32_t) * rom_bytes, cudaMemcpyHostToDevice);
   delete[] pre_host;

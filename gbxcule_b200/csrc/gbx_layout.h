@@ -69,7 +69,7 @@ enum StatusBits {
 };
 
 struct DevState {
-  const uint8_t* rom;     // [rom_bytes] shared, read-only
+  const uint8_t* rom;     // [rom_bytes + 16] shared, read-only (16 zero bytes of padding)
   const uint8_t* boot;    // [256]
   int32_t rom_bytes, rom_bank_count, rom_bank_mask, ram_bank_count;
   int32_t n, S;           // envs, SoA row stride

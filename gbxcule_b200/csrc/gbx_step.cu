@@ -674,6 +674,12 @@ struct Emu {
     return v | 0xC0;
   }
 
+  // JOYP's value for select bits 00, 10, 20, 30 (bytes 0..3); changes only
+  // when frames_done crosses the release frame
+  __device__ __forceinline__ uint32_t joyp_table() const {
+    return (uint32_t)joyp_value(0x00) | ((uint32_t)joyp_value(0x10) << 8) | ((uint32_t)joyp_value(0x20) << 16) |
+           ((uint32_t)joyp_value(0x30) << 24);
+  }
   // JOYP select write: the register latches the selected group's buttons
   __device__ __forceinline__ void write_joyp(int val) {
     const int sel = val & 0x30;
@@ -988,32 +994,48 @@ __device__ __forceinline__ int sign8(int v) { return v >= 128 ? v - 256 : v; }
 // fetches outside the staged words), the special opcodes and the exact
 // post-instruction tail, as in the switch loop. Same results, instruction for
 // instruction, as the switch loop (both follow the reference templates).
+// rom_s: raw bytes of ROM offsets [0, pre_s_words + 16) in shared memory as
+// words; rom_g: the whole ROM (zero-padded by 16 bytes) as words.
 template <int MBC>
 __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int& ninstr, int& win_hi,
-                                             int& bankN_off, int& cram_off, const uint32_t* pre_s,
-                                             const uint32_t* __restrict__ pre_g, int pre_s_words,
+                                             int& bankN_off, int& cram_off, const uint32_t* rom_s,
+                                             const uint32_t* __restrict__ rom_g, int pre_s_words,
                                              const uint8_t* dec_s, const uint4* ud_s, int frames_to_run) {
   uint8_t* const mem = s.mem;
   uint8_t* const cram = s.cart_ram;
-  // byte reads and writes: VRAM, WRAM, HRAM and the mapped cart-RAM bank as
-  // one predicated access; JOYP inline; the rest out of line
-  auto urd = [&](int a) -> int {
-    const bool pl = ((a >> 13) | 2) == 6 || (unsigned)(a - 0xFF80) < 0x7Fu;
-    const bool cr = (unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0;
-    const uint8_t* p = pl ? mem + a : cram + (cram_off + a - 0xA000);
-    if (pl || cr) return *p;
-    if (a == 0xFF00) return s.joyp;
+  // Byte accesses: VRAM, WRAM, HRAM and the mapped cart-RAM bank inline, JOYP
+  // from its register, everything else (IO, ROM, cartridge registers) out of
+  // line through the full memory map.
+  auto fast = [&](int a) {
+    return ((a >> 13) | 2) == 6 || (unsigned)(a - 0xFF80) < 0x7Fu ||
+           ((unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0);
+  };
+  auto fptr = [&](int a) -> uint8_t* {
+    return (unsigned)(a - 0xA000) < 0x2000u ? cram + (cram_off + a - 0xA000) : mem + a;
+  };
+  // JOYP in registers: its value and its value per select setting (the
+  // out-of-line paths see them through s.joyp, synced around each call)
+  int jp = s.joyp;
+  uint32_t jtab = s.joyp_table();
+  uint8_t* const jsel = s.u8s + (size_t)F_JOYP_SELECT * s.S;
+  auto joyp_write = [&](int v) {
+    jp = (int)((jtab >> ((v >> 1) & 0x18)) & 0xFF);
+    *jsel = (uint8_t)(v & 0x30);
+  };
+  auto urd = [&](int a) -> int {  // full path
+    if (fast(a)) return *fptr(a);
+    if (a == 0xFF00) return jp;
     s.clk = h.clk;
+    s.joyp = jp;
     return s.read_slow(a);
   };
-  auto uwr = [&](int a, int v) {
-    const bool pl = ((a >> 13) | 2) == 6 || (unsigned)(a - 0xFF80) < 0x7Fu;
-    const bool cr = (unsigned)(a - 0xA000) < 0x2000u && cram_off >= 0;
-    uint8_t* p = pl ? mem + a : cram + (cram_off + a - 0xA000);
-    if (pl || cr) { *p = (uint8_t)v; return; }
-    if (a == 0xFF00) { s.write_joyp(v); return; }
+  auto uwr = [&](int a, int v) {  // full path
+    if (fast(a)) { *fptr(a) = (uint8_t)v; return; }
+    if (a == 0xFF00) { joyp_write(v); return; }
     s.clk = h.clk;
+    s.joyp = jp;
     s.write_slow(a, v);
+    jp = s.joyp;
     h.clk = s.clk;
     if (s.ev) h.next_ev = INT_MIN;
     win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
@@ -1021,15 +1043,18 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
 
   while (run) {
     const int pc = h.pc;
-    // ---- fetch: staged words, the switched bank's words, or out of line ----
+    // ---- fetch: opcode and two operand bytes from the staged bytes or the
+    //      switched bank (the two aligned words around them), else out of line
     uint32_t w;
     {
       const bool ins = (unsigned)pc < (unsigned)win_hi;
       const bool inn = (unsigned)(pc - 0x4000) < 0x3FFEu && bankN_off >= 0;
       const int idx = ins ? pc : pc + bankN_off;
-      if (ins || (inn && idx < pre_s_words)) w = pre_s[idx];
-      else if (inn) w = __ldg(pre_g + idx);
-      else { s.clk = h.clk; w = s.fetch_slow(pc, dec_s); }
+      uint32_t lo, hi;
+      if (ins || (inn && idx < pre_s_words)) { lo = rom_s[idx >> 2]; hi = rom_s[(idx >> 2) + 1]; }
+      else if (inn) { lo = __ldg(rom_g + (idx >> 2)); hi = __ldg(rom_g + (idx >> 2) + 1); }
+      if (ins || inn) w = __funnelshift_r(lo, hi, (idx & 3) << 3);
+      else { s.clk = h.clk; s.joyp = jp; w = s.fetch_slow(pc, dec_s); }
     }
     const int op = w & 0xFF, b1 = (w >> 8) & 0xFF, imm16 = (w >> 8) & 0xFFFF;
     const int key = op == 0xCB ? 256 + b1 : op;
@@ -1047,9 +1072,13 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
     if (fa & UF_EA_FF) ea |= 0xFF00;
     ea = (ea - (int)((fa >> UF_EA_DEC_BIT) & 1)) & 0xFFFF;
     // ---- reads (the stack only when a conditional return is taken) ----
+    const int ea1 = (ea + 1) & 0xFFFF;
+    const bool rd1 = (fa & UF_RD1) && taken, rd2 = (fa & UF_RD2) && taken;
     int v0 = 0, v1 = 0;
-    if ((fa & UF_RD1) && taken) v0 = urd(ea);
-    if ((fa & UF_RD2) && taken) v1 = urd((ea + 1) & 0xFFFF);
+    // memory operands through branches taken by the lanes that have one
+    // (measured faster than issuing them predicated from the converged flow)
+    if (rd1) v0 = urd(ea);
+    if (rd2) v1 = urd(ea1);
     const int x = (fa & UF_X_MEM) ? v0 : (fa & UF_X_IMM) ? b1 : xr;
     // ---- adder: 8-bit ALU, INC/DEC, 16-bit pair arithmetic ----
     const int k16 = (int)(q0.y >> 16);
@@ -1091,18 +1120,16 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
     const int len = vx & 3;
     const int seq = pc + len;
     const int nw = (vx >> UV_NW) & 3;
-    if (nw && taken) {
-      int w0 = r8, a1 = 0, w1 = 0;
-      if (nw == 2) {
-        const int vs = (vy >> UY_VSRC) & 3;
-        const int val = vs == UVS_P16 ? p16 : vs == UVS_PCN ? (seq & 0xFFFF) : h.sp;
-        const bool lof = fa & UF_LOFIRST;
-        w0 = lof ? (val & 0xFF) : (val >> 8);
-        w1 = lof ? (val >> 8) : (val & 0xFF);
-        a1 = (ea + (lof ? 1 : -1)) & 0xFFFF;
-      }
-      uwr(ea, w0);
-      if (nw == 2) uwr(a1, w1);
+    {
+      const int vs = (vy >> UY_VSRC) & 3;
+      const int val = vs == UVS_P16 ? p16 : vs == UVS_PCN ? (seq & 0xFFFF) : h.sp;
+      const bool lof = fa & UF_LOFIRST;
+      const int w0 = nw == 2 ? (lof ? (val & 0xFF) : (val >> 8)) : r8;
+      const int w1 = lof ? (val >> 8) : (val & 0xFF);
+      const int a1 = lof ? ea1 : ((ea - 1) & 0xFFFF);
+      const bool wr0 = nw && taken, wr1 = nw == 2 && taken;
+      if (wr0) uwr(ea, w0);
+      if (wr1) uwr(a1, w1);
     }
     // ---- register results ----
     if (fa & UF_D8) {
@@ -1154,13 +1181,17 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
     if (h.clk >= h.next_ev) {
       if (s.trap) { ninstr--; break; }
       s.bcde = h.bcde; s.hlxa = h.hlxa; s.f = h.f; s.pc = h.pc; s.sp = h.sp; s.clk = h.clk;
+      s.joyp = jp;
       const bool done = s.tail_slow(cyc, op, pc, frames_to_run);
       h.bcde = s.bcde; h.hlxa = s.hlxa; h.f = s.f; h.pc = s.pc; h.sp = s.sp; h.clk = s.clk;
       h.next_ev = s.next_ev;
       win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
+      jp = s.joyp;
+      jtab = s.joyp_table();  // the frame count may have crossed the release frame
       if (done) break;
     }
   }
+  s.joyp = jp;
 }
 
 // ---------------------------------------------------------------------------
@@ -1173,25 +1204,28 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
 // DBG = the debug-trap instantiation (launched only when a trap is set).
 // UNI = the uniform-datapath interpreter (gbx_udesc.h) in place of the
 // per-family switch: for full warps of envs at different PCs.
-// Shared memory: pre-decoded ROM words | boot ROM | family table | (UNI)
-// descriptor table at the next 16-byte boundary.
-__host__ __device__ constexpr size_t udesc_smem_offset(int pre_s_words) {
-  return ((size_t)pre_s_words * 4 + 512 + 15) & ~(size_t)15;
+// Shared memory, switch: pre-decoded words of ROM offsets [0, P) | boot ROM |
+// family table. Uniform: raw ROM bytes [0, P + 16) | boot ROM | family table
+// | descriptor table. P = staged ROM offsets (pre_s_words).
+__host__ __device__ constexpr size_t rom_smem_bytes(int P, bool uni) {
+  return uni ? (((size_t)P + 16 + 15) & ~(size_t)15) : (size_t)P * 4;
 }
+__host__ __device__ constexpr size_t udesc_smem_offset(int P) { return rom_smem_bytes(P, true) + 512; }
 template <int MBC, int MAXT, bool DBG, bool UNI>
 __global__ void __launch_bounds__(MAXT, 1)
     gb_step_kernel(DevState st, const uint32_t* __restrict__ pre_g, const int32_t* __restrict__ actions,
                    int frames_to_run, int release_after_frames, int stage, int K, int pre_s_words,
                    DebugCfg dbg) {
   extern __shared__ __align__(16) uint8_t smem[];
-  uint32_t* pre_s = reinterpret_cast<uint32_t*>(smem);
-  uint8_t* boot_s = smem + (size_t)pre_s_words * 4;
+  uint32_t* pre_s = reinterpret_cast<uint32_t*>(smem);  // words (switch) or raw bytes (uniform)
+  uint8_t* boot_s = smem + rom_smem_bytes(pre_s_words, UNI);
   uint8_t* dec_s = boot_s + 256;
   uint4* ud_s = reinterpret_cast<uint4*>(smem + udesc_smem_offset(pre_s_words));
   {
-    const uint4* src = reinterpret_cast<const uint4*>(pre_g);
+    const uint4* src = UNI ? reinterpret_cast<const uint4*>(st.rom) : reinterpret_cast<const uint4*>(pre_g);
     uint4* dst = reinterpret_cast<uint4*>(pre_s);
-    for (int k = threadIdx.x; k < pre_s_words / 4; k += blockDim.x) dst[k] = __ldg(src + k);
+    const int n16 = (int)(rom_smem_bytes(pre_s_words, UNI) / 16);
+    for (int k = threadIdx.x; k < n16; k += blockDim.x) dst[k] = __ldg(src + k);
     for (int k = threadIdx.x; k < 256; k += blockDim.x) {
       boot_s[k] = st.boot[k];
       dec_s[k] = c_decode.e[k];
@@ -1335,8 +1369,8 @@ __global__ void __launch_bounds__(MAXT, 1)
   };
 
   if constexpr (UNI) {
-    uniform_loop<MBC>(s, h, run, ninstr, win_hi, bankN_off, cram_off, pre_s, pre_g, pre_s_words, dec_s, ud_s,
-                      frames_to_run);
+    uniform_loop<MBC>(s, h, run, ninstr, win_hi, bankN_off, cram_off, pre_s,
+                      reinterpret_cast<const uint32_t*>(st.rom), pre_s_words, dec_s, ud_s, frames_to_run);
   } else while (run) {
     // ---- fetch + decode ----
     const int pc = h.pc;
@@ -1753,6 +1787,14 @@ static cudaError_t launch_t(const DevState& st, const uint32_t* pre, const int32
   cudaError_t e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT, DBG, UNI>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
+  // GBX_SMEM_CARVEOUT (percent of the unified L1/shared storage given to
+  // shared memory, experiments): unset = the driver's choice
+  const int carve = env_int("GBX_SMEM_CARVEOUT", -1);
+  if (carve >= 0) {
+    e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT, DBG, UNI>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             carve > 100 ? 100 : carve);
+    if (e != cudaSuccess) return e;
+  }
   gb_step_kernel<MBC, MAXT, DBG, UNI><<<blocks, threads, sm, stream>>>(st, pre, actions, frames, release, stage,
                                                                       K, pre_s_words, dbg);
   return cudaGetLastError();

@@ -158,11 +158,12 @@ int gbx_step(gbx_env* env, const int32_t* actions, int32_t frames_to_run,
  * default; GBX_ENVS_PER_WARP in the environment fixes it for every handle).
  * No counterpart in the reference, whose Warp launch maps one env per thread
  * with Warp's own block size. K never changes a result, only speed. In
- * automatic mode the first 4 or 6 real steps of the handle each run with one
- * of up to three candidates (the K that fills one wave of warps on the
- * device, half of it, and 32), timed with CUDA events around the launches
- * the caller requested, and later steps use the fastest. Synchronises the
- * device. */
+ * automatic mode the handle's first real steps each run with one candidate
+ * launch shape, twice per candidate (K: the one that fills one wave of warps
+ * on the device, half of it, and 32; interpreter: the switch at each K and
+ * the uniform datapath at each K >= 16, unless gbx_set_dispatch fixes it),
+ * timed with CUDA events around the launches the caller requested, and
+ * later steps use the fastest. Synchronises the device. */
 int gbx_set_envs_per_warp(gbx_env* env, int32_t envs_per_warp);
 
 /* Interpreter of the step kernel: GBX_DISPATCH_SWITCH (one switch case per
