@@ -792,7 +792,13 @@ struct Emu {
       if (off >= 0) cart_ram[off] = (uint8_t)v8;
       return;
     }
-    if (a < 0x8000) {
+    if (a < 0x8000) { write_mbc(a, val); return; }
+    M(a) = (uint8_t)v8;  // FE00-FEFF
+  }
+
+  // cartridge register write (0000-7FFF): RAM enable, bank selects, RTC latch
+  __device__ __forceinline__ void write_mbc(int a, int val) {
+    {
       if (MBC == MBC_MBC1) {
         if (a < 0x2000) ram_en = (val & 0x0F) == 0x0A;
         else if (a < 0x4000) { int b = val & 0x1F; bank_lo = b ? b : 1; }
@@ -812,9 +818,7 @@ struct Emu {
         }
         update_banks();
       }
-      return;
     }
-    M(a) = (uint8_t)v8;  // FE00-FEFF
   }
 
   __device__ __forceinline__ void write8(int addr, int val) {
@@ -1025,6 +1029,7 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
   auto urd = [&](int a) -> int {  // full path
     if (fast(a)) return *fptr(a);
     if (a == 0xFF00) return jp;
+    if (a < 0x8000) return s.rom_read(a);  // cartridge ROM, banked (no call)
     s.clk = h.clk;
     s.joyp = jp;
     return s.read_slow(a);
@@ -1032,6 +1037,11 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
   auto uwr = [&](int a, int v) {  // full path
     if (fast(a)) { *fptr(a) = (uint8_t)v; return; }
     if (a == 0xFF00) { joyp_write(v); return; }
+    if (a < 0x8000) {  // cartridge registers: banking state only (no call, no timing)
+      s.write_mbc(a, v);
+      win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
+      return;
+    }
     s.clk = h.clk;
     s.joyp = jp;
     s.write_slow(a, v);
@@ -1077,8 +1087,10 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
     int v0 = 0, v1 = 0;
     // memory operands through branches taken by the lanes that have one
     // (measured faster than issuing them predicated from the converged flow)
-    if (rd1) v0 = urd(ea);
-    if (rd2) v1 = urd(ea1);
+    if (rd1) {  // the second byte (POP, RET) only with the first
+      v0 = urd(ea);
+      if (rd2) v1 = urd(ea1);
+    }
     const int x = (fa & UF_X_MEM) ? v0 : (fa & UF_X_IMM) ? b1 : xr;
     // ---- adder: 8-bit ALU, INC/DEC, 16-bit pair arithmetic ----
     const int k16 = (int)(q0.y >> 16);
@@ -1128,8 +1140,10 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
       const int w1 = lof ? (val >> 8) : (val & 0xFF);
       const int a1 = lof ? ea1 : ((ea - 1) & 0xFFFF);
       const bool wr0 = nw && taken, wr1 = nw == 2 && taken;
-      if (wr0) uwr(ea, w0);
-      if (wr1) uwr(a1, w1);
+      if (wr0) {
+        uwr(ea, w0);
+        if (wr1) uwr(a1, w1);
+      }
     }
     // ---- register results ----
     if (fa & UF_D8) {
