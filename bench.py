@@ -374,11 +374,12 @@ def run_config5(args) -> None:
     masks_host = (mrng.random((W + 2 * K, n)) < RESTORE_RATE).astype(np.uint8)
     masks_dev = torch.as_tensor(masks_host[:W + K], device=dev)
     run_rollout(be, pol, W, generator=gen, reset_cache=cache, reset_mask=lambda k: masks_dev[k], packed_out=packed)
-    i64 = be._view("i64")  # row 0: per-env emulated instruction counters
+    # SM83 instructions of the timed steps, summed on the device around each
+    # step (a restore copies the snapshot's counters into the restored envs)
+    instr_acc = torch.zeros((), dtype=torch.int64, device=dev)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    ninstr0 = int(i64[0].sum())
     clocks = ClockSampler(local)
     clocks.start()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
@@ -386,15 +387,16 @@ def run_config5(args) -> None:
     wall0 = time.perf_counter()
     e0.record()
     run_rollout(be, pol, K, generator=gen, reset_cache=cache, reset_mask=lambda k: masks_dev[W + k],
-                packed_out=packed, step_events=ev)
+                packed_out=packed, step_events=ev, instr_acc=instr_acc)
     e1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
     clk = clocks.stop()
     total_ms = e0.elapsed_time(e1)
     step_ms = [a.elapsed_time(b) for a, b in ev]
-    ninstr = int(i64[0].sum()) - ninstr0
+    ninstr = int(instr_acc)
     k_used, k_settled = be.envs_per_warp()
+    dispatch = be.dispatch()
 
     # end to end through the public API with host buffers: the reset mask in
     # from pinned memory, the packed frames and sampled actions out
@@ -441,7 +443,7 @@ def run_config5(args) -> None:
                    "l2": "inputs larger than L2: 12.7 GB of per-env state per GPU (64 KiB address space + "
                          "32 KiB cart RAM + 1 KiB serial per env), no flush",
                    "parallelism": f"{ws} independent env slices, no collective on the step path",
-                   "envs_per_warp": k_used, "envs_per_warp_settled": k_settled},
+                   "envs_per_warp": k_used, "envs_per_warp_settled": k_settled, "dispatch": dispatch},
         "emulated_frames_per_s": value * FRAMES,
         "emulated_instr_per_s": ninstr / (total_ms / 1e3),
         "emulated_instr_per_env_step": ninstr / (n * ws * K),

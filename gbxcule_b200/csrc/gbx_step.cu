@@ -1004,7 +1004,8 @@ template <int MBC>
 __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int& ninstr, int& win_hi,
                                              int& bankN_off, int& cram_off, const uint32_t* rom_s,
                                              const uint32_t* __restrict__ rom_g, int pre_s_words,
-                                             const uint8_t* dec_s, const uint4* ud_s, int frames_to_run) {
+                                             const uint8_t* dec_s, const uint4* ud_s, int frames_to_run,
+                                             unsigned alive) {
   uint8_t* const mem = s.mem;
   uint8_t* const cram = s.cart_ram;
   // Byte accesses: VRAM, WRAM, HRAM and the mapped cart-RAM bank inline, JOYP
@@ -1051,7 +1052,16 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
     win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
   };
 
-  while (run) {
+  // Warp-synchronous loop: every live lane of the warp meets at the vote at
+  // the end of each iteration, finished lanes included (their body is
+  // skipped). Without this convergence point the lanes drift out of lockstep
+  // when freshly restored envs are spread over the warps: on config 5 with 5 %
+  // random restores per step the free loop issued 412 G warp instructions at
+  // 14.7 active lanes against 318 G at 19.1 with the same restores packed into
+  // the first warps (same emulated instructions); with the vote the step went
+  // 566 -> 470 ms, at a 6 % cost (441 -> 470 ms) where no env is restored.
+  for (;;) {
+    if (run) {
     const int pc = h.pc;
     // ---- fetch: opcode and two operand bytes from the staged bytes or the
     //      switched bank (the two aligned words around them), else out of line
@@ -1192,18 +1202,25 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
     // ---- tail ----
     ninstr++;
     h.clk += cyc;
+    bool stop = false;
     if (h.clk >= h.next_ev) {
-      if (s.trap) { ninstr--; break; }
-      s.bcde = h.bcde; s.hlxa = h.hlxa; s.f = h.f; s.pc = h.pc; s.sp = h.sp; s.clk = h.clk;
-      s.joyp = jp;
-      const bool done = s.tail_slow(cyc, op, pc, frames_to_run);
-      h.bcde = s.bcde; h.hlxa = s.hlxa; h.f = s.f; h.pc = s.pc; h.sp = s.sp; h.clk = s.clk;
-      h.next_ev = s.next_ev;
-      win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
-      jp = s.joyp;
-      jtab = s.joyp_table();  // the frame count may have crossed the release frame
-      if (done) break;
+      if (s.trap) {
+        ninstr--;
+        stop = true;
+      } else {
+        s.bcde = h.bcde; s.hlxa = h.hlxa; s.f = h.f; s.pc = h.pc; s.sp = h.sp; s.clk = h.clk;
+        s.joyp = jp;
+        stop = s.tail_slow(cyc, op, pc, frames_to_run);
+        h.bcde = s.bcde; h.hlxa = s.hlxa; h.f = s.f; h.pc = s.pc; h.sp = s.sp; h.clk = s.clk;
+        h.next_ev = s.next_ev;
+        win_hi = s.win_hi; bankN_off = s.bankN_off; cram_off = s.cram_off;
+        jp = s.joyp;
+        jtab = s.joyp_table();  // the frame count may have crossed the release frame
+      }
     }
+    if (stop) run = false;
+    }
+    if (!__any_sync(alive, run)) break;
   }
   s.joyp = jp;
 }
@@ -1211,7 +1228,8 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-// K = envs per warp: lane l < K of global warp w runs env w*K + l. Small K
+// K = envs per warp: lane l < K of global warp w runs env w*K + l (K = 1),
+// or env 0 alone in warp 0 and env 1 + (w-1)*K + l in warp w >= 1. Small K
 // spreads few envs over many warps (no divergence, more latency hiding);
 // K = 32 packs a full warp (shared issue slots when envs run in lockstep).
 // MAXT = largest block size the launch may use (caps registers at 64K/MAXT).
@@ -1251,9 +1269,14 @@ __global__ void __launch_bounds__(MAXT, 1)
   }
   __syncthreads();
 
+  // Env 0 alone takes the exact post-instruction path at every scanline (it
+  // records the scanline latches), so with K > 1 it gets warp 0 to itself and
+  // no other env waits on it; lane l of warp w >= 1 runs env 1 + (w-1)*K + l.
   const int lane = threadIdx.x & 31;
   if (lane >= K) return;
-  const int env = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * K + lane;
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (K > 1 && gw == 0 && lane != 0) return;
+  const int env = K == 1 ? gw : gw == 0 ? 0 : 1 + (gw - 1) * K + lane;
   if (env >= st.n) return;
   const size_t S = (size_t)st.S;
 
@@ -1383,8 +1406,14 @@ __global__ void __launch_bounds__(MAXT, 1)
   };
 
   if constexpr (UNI) {
+    // lanes of this warp that run an env (the others returned above)
+    unsigned alive = 0;
+    for (int l = 0; l < K; l++) {
+      const int e = K == 1 ? gw : gw == 0 ? (l == 0 ? 0 : st.n) : 1 + (gw - 1) * K + l;
+      if (e < st.n) alive |= 1u << l;
+    }
     uniform_loop<MBC>(s, h, run, ninstr, win_hi, bankN_off, cram_off, pre_s,
-                      reinterpret_cast<const uint32_t*>(st.rom), pre_s_words, dec_s, ud_s, frames_to_run);
+                      reinterpret_cast<const uint32_t*>(st.rom), pre_s_words, dec_s, ud_s, frames_to_run, alive);
   } else while (run) {
     // ---- fetch + decode ----
     const int pc = h.pc;
@@ -1820,7 +1849,7 @@ static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int
                               int sms, bool uniform) {
   K = K < 1 ? 1 : K > 32 ? 32 : K;
   sms = sms < 1 ? 1 : sms;
-  const long long warps = (st.n + K - 1) / K;
+  const long long warps = K == 1 ? st.n : 1 + (st.n - 1 + K - 1) / K;  // env 0 in a warp of its own
   // one block per SM (the pre-decoded banks fill shared memory): spread warps
   int per_block = (int)((warps + sms - 1) / sms);
   per_block = per_block < 1 ? 1 : per_block > WARPS_PER_SM ? WARPS_PER_SM : per_block;

@@ -107,7 +107,7 @@ class Rollout:
 
 def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 16384,
                 reset_cache=None, reset_mask: Callable[[int], Any] | None = None,
-                packed_out=None, step_events=None, host_out=None) -> Rollout:
+                packed_out=None, step_events=None, host_out=None, instr_acc=None) -> Rollout:
     """``steps`` env-steps of render -> unpack -> policy -> sample -> step.
 
     ``reset_mask(k)`` (a CUDA bool/uint8 [N] or None) selects envs restored
@@ -116,7 +116,10 @@ def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 163
     events, optional) is recorded around step k's ``step_torch``.
     ``host_out`` (optional pair of pinned host tensors, [2, N, 72, 20] uint8
     and [2, N] int32) receives each step's packed frames and sampled actions,
-    copied asynchronously into slot k % 2. Returns the sampled actions (and
+    copied asynchronously into slot k % 2. ``instr_acc`` (optional int64
+    CUDA scalar) accumulates the SM83 instructions each step executed, read
+    from the per-env counters around the step and before any restore (a
+    restore copies the snapshot's counters). Returns the sampled actions (and
     masks).
     """
     import torch
@@ -136,11 +139,15 @@ def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 163
             if host_out is not None:
                 host_out[0][k % 2].copy_(packed, non_blocking=True)
                 host_out[1][k % 2].copy_(acts, non_blocking=True)
+            if instr_acc is not None:
+                instr_acc -= backend._view("i64")[0].sum()
             if step_events is not None:
                 step_events[k][0].record()
             backend.step_torch(acts)
             if step_events is not None:
                 step_events[k][1].record()
+            if instr_acc is not None:
+                instr_acc += backend._view("i64")[0].sum()
             out.actions.append(acts)
             mask = reset_mask(k) if reset_mask is not None else None
             if mask is not None and reset_cache is not None:
