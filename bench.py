@@ -76,16 +76,17 @@ WORKLOADS = {
 }
 
 # smsp__inst_executed.sum / emulated SM83 instructions of one step-kernel
-# launch, from the committed ncu captures named beside each value (the
-# integer-issue cost of one emulated instruction at this workload's envs per
-# warp). tests/test_bench_cpu.py checks these against the profile summaries.
+# launch, per workload and interpreter, from the committed ncu captures named
+# beside each value (the integer-issue cost of one emulated instruction).
+# tests/test_bench_cpu.py checks these against the profile summaries. A shape
+# without a capture reports no issue roof.
 WARP_INSTR_PER_EMULATED_INSTR = {
-    "config5": (128.473475553e9 / (32768 * 149430), "profiles/gb_step_kernel_config5_32768envs.md"),
-    "config2": (48.096002450e9 / (4096 * 197327.3), "profiles/gb_step_kernel_config2_4096envs.md"),
+    "config5:uniform": (336.912659579e9 / (131072 * 193219.985), "profiles/gb_step_kernel_uniform_config5_131072envs.md"),
+    "config2:switch": (48.096002450e9 / (4096 * 197327.3), "profiles/gb_step_kernel_config2_4096envs.md"),
 }
 # dram__bytes_read.sum + dram__bytes_write.sum per env of one step-kernel
 # launch, from the same captures (None: not captured for this build).
-STEP_DRAM_BYTES_PER_ENV = {"config5": (63.113221e9 + 13.347018e9) / 32768, "config2": None}
+STEP_DRAM_BYTES_PER_ENV = {"config5:uniform": (332.06e9 + 69.45e9) / 131072, "config2:switch": None}
 
 # Per-env state the step kernel reads at launch start and writes back at the
 # end (27 i32 + 2 i64 + 3 u8 scalars, 20 i32 cart_state words, 12 cached IO
@@ -187,14 +188,15 @@ def step_bytes(cfg: int, ram_ops_per_env_step: float, restore_rate: float) -> fl
             + restore_rate * RESTORE_BYTES.get(cfg, 0))
 
 
-def roofline(workload: str, cfg: int, envs: int, kernel_ms: float, emu_instr_per_launch: float,
+def roofline(shape: str, cfg: int, envs: int, kernel_ms: float, emu_instr_per_launch: float,
              ram_ops_per_env_step: float | None, sm_count: int, sm_mhz: float | None,
              restore_rate: float) -> dict:
-    """Both roofs of the step kernel; ``bound`` is the one with the larger fraction."""
+    """Both roofs of the step kernel; ``bound`` is the one with the larger
+    fraction. ``shape`` = "<workload>:<interpreter>" of the timed launches."""
     peaks = _peaks()
     mhz = sm_mhz or 1965.0
     secs = kernel_ms / 1e3
-    wipe, wsrc = WARP_INSTR_PER_EMULATED_INSTR[workload]
+    wipe, wsrc = WARP_INSTR_PER_EMULATED_INSTR.get(shape, (None, None))
     issue = None
     if wipe:
         ach = wipe * emu_instr_per_launch / secs
@@ -206,18 +208,18 @@ def roofline(workload: str, cfg: int, envs: int, kernel_ms: float, emu_instr_per
     if ram_ops_per_env_step is not None:
         b = step_bytes(cfg, ram_ops_per_env_step, restore_rate)
         ach = b * envs / secs / 1e9
-        dram = STEP_DRAM_BYTES_PER_ENV.get(workload)
+        dram = STEP_DRAM_BYTES_PER_ENV.get(shape)
         hbm = {"achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
                "bytes_per_env_step": b, "ram_ops_bytes_per_env_step": ram_ops_per_env_step,
                "peak_source": peaks["source"],
                "traffic": None if dram is None else dram * envs}
     cands = [(r["frac"], name, r) for name, r in (("integer-issue", issue), ("hbm", hbm)) if r]
     if not cands:
-        return {"bound": None, "kernel": "gb_step_kernel", "kernel_ms": kernel_ms}
+        return {"bound": None, "kernel": "gb_step_kernel", "kernel_ms": kernel_ms, "shape": shape}
     frac, name, r = max(cands, key=lambda t: t[0])
     out = {"bound": name, "achieved": r["achieved"], "peak": r["peak"], "unit": r["unit"], "frac": frac,
            "traffic": hbm["traffic"] if hbm else None, "kernel": "gb_step_kernel", "kernel_ms": kernel_ms,
-           "emulated_instr_per_launch": emu_instr_per_launch}
+           "emulated_instr_per_launch": emu_instr_per_launch, "shape": shape}
     out["issue"] = issue
     out["hbm"] = hbm
     return out
@@ -450,7 +452,7 @@ def run_config5(args) -> None:
         "step_kernel_ms": step_avg_ms,
         "e2e": {"value": job_rate(n, ws, K, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": n,
                 "d2h_bytes_per_step": n * (72 * 20 + 4)},
-        "roofline": roofline("config5", 5, n, step_avg_ms, ninstr / (ws * K),
+        "roofline": roofline(f"config5:{dispatch}", 5, n, step_avg_ms, ninstr / (ws * K),
                              cpu["ram_ops_bytes_per_env_step"] if cpu else None, sm_count,
                              clk.get("sm_mhz"), RESTORE_RATE),
         "clocks": clk,
@@ -513,6 +515,7 @@ def run_config2(args) -> None:
     total_ms = sum(s.elapsed_time(e) for s, _, e in ev)
     ninstr = int(i64[0].sum()) - ninstr0
     k_used, k_settled = be.envs_per_warp()
+    dispatch = be.dispatch()
 
     acts_pin = torch.from_numpy(acts_host[W + K:W + 2 * K]).pin_memory()
     out_dev = torch.empty((n, 72, 20), dtype=torch.uint8, device=dev)
@@ -551,14 +554,14 @@ def run_config2(args) -> None:
                    "release_after_frames": RELEASE,
                    "l2": "read-only 256 MiB sweep between timed steps (outside the events)",
                    "parallelism": f"{ws} independent env slices, no collective on the step path",
-                   "envs_per_warp": k_used, "envs_per_warp_settled": k_settled},
+                   "envs_per_warp": k_used, "envs_per_warp_settled": k_settled, "dispatch": dispatch},
         "emulated_frames_per_s": value * FRAMES,
         "emulated_instr_per_s": ninstr / (step_avg_ms * K / 1e3),
         "emulated_instr_per_env_step": ninstr / (n * ws * K),
         "step_kernel_ms": step_avg_ms,
         "e2e": {"value": job_rate(n, ws, K, e2e_ms), "unit": UNIT, "h2d_bytes_per_step": 4 * n,
                 "d2h_bytes_per_step": 72 * 20 * n},
-        "roofline": roofline("config2", 2, n, step_avg_ms, ninstr / (ws * K),
+        "roofline": roofline(f"config2:{dispatch}", 2, n, step_avg_ms, ninstr / (ws * K),
                              cpu["ram_ops_bytes_per_env_step"] if cpu else None, sm_count,
                              clk.get("sm_mhz"), 0.0),
         "clocks": clk,

@@ -33,14 +33,18 @@ def test_step_bytes_terms():
 
 
 def test_roofline_names_the_larger_fraction(monkeypatch):
-    monkeypatch.setitem(bench.WARP_INSTR_PER_EMULATED_INSTR, "config5", (10.0, "x"))
-    r = bench.roofline("config5", 5, 1000, kernel_ms=100.0, emu_instr_per_launch=1e9,
+    monkeypatch.setitem(bench.WARP_INSTR_PER_EMULATED_INSTR, "config5:uniform", (10.0, "x"))
+    r = bench.roofline("config5:uniform", 5, 1000, kernel_ms=100.0, emu_instr_per_launch=1e9,
                        ram_ops_per_env_step=5e4, sm_count=148, sm_mhz=2000.0, restore_rate=0.05)
     issue = 10.0 * 1e9 / 0.1 / (148 * 4 * 2000e6)
     assert r["issue"]["frac"] == pytest.approx(issue)
     assert r["bound"] == ("integer-issue" if issue > r["hbm"]["frac"] else "hbm")
     assert r["frac"] == pytest.approx(max(issue, r["hbm"]["frac"]))
     json.dumps(r)
+    # a shape without a committed capture has no issue roof
+    r2 = bench.roofline("config5:switch", 5, 1000, kernel_ms=100.0, emu_instr_per_launch=1e9,
+                        ram_ops_per_env_step=5e4, sm_count=148, sm_mhz=2000.0, restore_rate=0.05)
+    assert r2["issue"] is None and r2["bound"] == "hbm"
 
 
 def _profile_ratio(path: Path) -> float:
