@@ -13,7 +13,7 @@ import ctypes
 from ctypes import POINTER, c_char_p, c_int32, c_int64, c_size_t, c_uint32, c_void_p
 
 GBX_OK, GBX_ERR_INVALID, GBX_ERR_CUDA, GBX_ERR_OOM, GBX_ERR_STATE, GBX_ERR_RANGE = range(6)
-ABI_VERSION = 4  # include/gbx.h GBX_ABI_VERSION
+ABI_VERSION = 5  # include/gbx.h GBX_ABI_VERSION
 
 BUF = {"mem": 0, "pixels": 1, "pixels_packed": 2, "obs": 3, "reward": 4, "cart_ram": 5,
        "serial": 6, "i32": 7, "i64": 8, "u8": 9, "cart_state": 10, "latch": 11, "frame_bg": 12}
@@ -75,6 +75,7 @@ def lib():
         "gbx_reset": ([P, P], c_int32),
         "gbx_step": ([P, P, c_int32, c_int32, P], c_int32),
         "gbx_render_packed": ([P, P, c_int64, P], c_int32),
+        "gbx_render_packed_scaled": ([P, P, c_int64, P, P], c_int32),
         "gbx_render_shades": ([P, P, P], c_int32),
         "gbx_snapshot_create": ([P, c_int32, P, E], c_int32),
         "gbx_snapshot_destroy": ([P], c_int32),

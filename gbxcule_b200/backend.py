@@ -324,6 +324,39 @@ class GbxVecCudaBackend:
         L.check(self._lib.gbx_render_packed(self._h, ctypes.c_void_p(out.data_ptr()), int(base_offset_bytes),
                                             self._stream()), "gbx_render_packed")
 
+    def render_pixels_snapshot_packed_scaled_to_torch(self, out, scaled, base_offset_bytes: int = 0) -> None:
+        """``render_pixels_snapshot_packed_to_torch`` plus the policy input in
+        the same launch: ``scaled`` (CUDA bf16, contiguous, >= N*72*80
+        elements) receives every pixel as shade / 3.0 in bf16, the tensor a
+        consumer gets from unpacking the packed bytes (rl/packed_pixels.py:26-71)
+        and dividing by 3.0. ``out`` may be None (the backend's own packed
+        buffer)."""
+        if not self._initialized or self._h is None:
+            raise RuntimeError("Backend not initialized. Call reset() first.")
+        torch = self._torch()
+        if not isinstance(scaled, torch.Tensor):
+            raise TypeError("scaled must be a torch.Tensor")
+        if scaled.device.type != "cuda" or scaled.dtype is not torch.bfloat16 or not scaled.is_contiguous():
+            raise ValueError("scaled must be a contiguous CUDA bfloat16 tensor")
+        if int(scaled.numel()) < self.num_envs * DOWNSAMPLE_H * DOWNSAMPLE_W_BYTES * 4:
+            raise ValueError("scaled does not have enough capacity for the frames")
+        ptr = None
+        if out is not None:
+            if not isinstance(out, torch.Tensor):
+                raise TypeError("out must be a torch.Tensor")
+            if out.device.type != "cuda" or out.dtype is not torch.uint8 or not out.is_contiguous():
+                raise ValueError("out must be a contiguous CUDA uint8 tensor")
+            if base_offset_bytes < 0:
+                raise ValueError("base_offset_bytes must be >= 0")
+            if base_offset_bytes + self.num_envs * DOWNSAMPLE_W_BYTES * DOWNSAMPLE_H > int(out.numel()):
+                raise ValueError("out does not have enough capacity for packed frame")
+            ptr = ctypes.c_void_p(out.data_ptr())
+        if self._force_lcdc_on_render:
+            self._apply_lcdc_override()
+        L.check(self._lib.gbx_render_packed_scaled(self._h, ptr, int(base_offset_bytes),
+                                                   ctypes.c_void_p(scaled.data_ptr()), self._stream()),
+                "gbx_render_packed_scaled")
+
     def pixels_torch(self):
         """[N, 72, 80] uint8 view of the shade buffer (warp_vec.py:865-876)."""
         if self._h is None or not self._initialized or not self._render_pixels:

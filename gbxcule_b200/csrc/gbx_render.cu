@@ -29,9 +29,14 @@ constexpr int RENDER_THREADS = 128;
 constexpr int MAX_SPR = 10;
 constexpr int OUT_ROWS = 72;
 
+// scaled (packed renders only, may be null): the same image as the policy
+// input a consumer builds from the packed bytes (unpack, to bf16, / 3.0), one
+// bf16 per pixel [N][72][80]; scale_tab holds the bf16 bits of shade / 3 for
+// shades 0..3 (16 bits each).
 template <bool PACKED>
 __global__ void __launch_bounds__(RENDER_THREADS) render_kernel(DevState st, uint8_t* __restrict__ out,
-                                                               int64_t base_offset, int vec) {
+                                                               int64_t base_offset, int vec,
+                                                               uint16_t* __restrict__ scaled, uint64_t scale_tab) {
   constexpr int BPR = PACKED ? 20 : 80;  // output bytes per row
   constexpr int ENV_BYTES = OUT_ROWS * BPR;
   __shared__ __align__(16) uint8_t vram[0x2000];
@@ -131,6 +136,14 @@ __global__ void __launch_bounds__(RENDER_THREADS) render_kernel(DevState st, uin
       packed |= (shade & 3) << (2 * k);
     }
     img[i] = (uint8_t)packed;
+    if (PACKED && scaled) {  // four pixels = one 8-byte store, consecutive threads adjacent
+      uint2 v;
+      v.x = (uint32_t)((scale_tab >> (16 * (packed & 3))) & 0xFFFF) |
+            ((uint32_t)((scale_tab >> (16 * ((packed >> 2) & 3))) & 0xFFFF) << 16);
+      v.y = (uint32_t)((scale_tab >> (16 * ((packed >> 4) & 3))) & 0xFFFF) |
+            ((uint32_t)((scale_tab >> (16 * ((packed >> 6) & 3))) & 0xFFFF) << 16);
+      reinterpret_cast<uint2*>(scaled + (size_t)env * (OUT_ROWS * 80))[i] = v;
+    }
   }
   __syncthreads();
   uint8_t* dst = out + base_offset + (int64_t)env * ENV_BYTES;
@@ -222,11 +235,13 @@ cudaError_t launch_render_bg_env0(const DevState& st, uint8_t* out, cudaStream_t
 }
 
 cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, uint16_t* scaled, uint64_t scale_tab) {
   // every env image starts 16-byte aligned when the buffer start is (1440 and 5760 are multiples of 16)
   const int vec = ((reinterpret_cast<uintptr_t>(out) + (uintptr_t)base_offset) & 15) == 0;
-  if (packed) render_kernel<true><<<st.n, RENDER_THREADS, 0, stream>>>(st, out, base_offset, vec);
-  else render_kernel<false><<<st.n, RENDER_THREADS, 0, stream>>>(st, out, base_offset, vec);
+  if (packed)
+    render_kernel<true><<<st.n, RENDER_THREADS, 0, stream>>>(st, out, base_offset, vec, scaled, scale_tab);
+  else
+    render_kernel<false><<<st.n, RENDER_THREADS, 0, stream>>>(st, out, base_offset, vec, nullptr, 0);
   return cudaGetLastError();
 }
 

@@ -994,12 +994,15 @@ __device__ __forceinline__ int sign8(int v) { return v >= 128 ? v - 256 : v; }
 // Every lane runs the same stages for its own instruction: fetch, descriptor,
 // operands, effective address, reads, adder / logic / rotate units, register,
 // flag and memory results, PC, SP and cycles. Divergence is left to the
-// memory accesses that miss the inline fast path (IO, cartridge registers,
-// fetches outside the staged words), the special opcodes and the exact
-// post-instruction tail, as in the switch loop. Same results, instruction for
-// instruction, as the switch loop (both follow the reference templates).
+// memory operands (a branch taken by the lanes that have one), the accesses
+// outside RAM (IO out of line; JOYP, banked ROM and cartridge registers
+// inline in that branch), fetches outside the staged and switched-bank
+// bytes, the special opcodes and the exact post-instruction tail. Same
+// results, instruction for instruction, as the switch loop (both follow the
+// reference templates).
 // rom_s: raw bytes of ROM offsets [0, pre_s_words + 16) in shared memory as
-// words; rom_g: the whole ROM (zero-padded by 16 bytes) as words.
+// words; rom_g: the whole ROM (zero-padded by 16 bytes) as words; alive: the
+// lanes of this warp that run an env (each must reach the loop's vote).
 template <int MBC>
 __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int& ninstr, int& win_hi,
                                              int& bankN_off, int& cram_off, const uint32_t* rom_s,
@@ -1070,11 +1073,16 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
       const bool ins = (unsigned)pc < (unsigned)win_hi;
       const bool inn = (unsigned)(pc - 0x4000) < 0x3FFEu && bankN_off >= 0;
       const int idx = ins ? pc : pc + bankN_off;
-      uint32_t lo, hi;
-      if (ins || (inn && idx < pre_s_words)) { lo = rom_s[idx >> 2]; hi = rom_s[(idx >> 2) + 1]; }
-      else if (inn) { lo = __ldg(rom_g + (idx >> 2)); hi = __ldg(rom_g + (idx >> 2) + 1); }
-      if (ins || inn) w = __funnelshift_r(lo, hi, (idx & 3) << 3);
-      else { s.clk = h.clk; s.joyp = jp; w = s.fetch_slow(pc, dec_s); }
+      // both loads predicated, no branch between the staged and switched-bank
+      // lanes (461 vs 470 ms on the config-5 bench step)
+      const bool sm = ins || (inn && idx < pre_s_words);
+      const bool gl = !sm && inn;
+      const int wi = (sm || gl) ? (idx >> 2) : 0;
+      uint32_t lo = 0, hi = 0;
+      if (sm) { lo = rom_s[wi]; hi = rom_s[wi + 1]; }
+      if (gl) { lo = __ldg(rom_g + wi); hi = __ldg(rom_g + wi + 1); }
+      w = __funnelshift_r(lo, hi, (idx & 3) << 3);
+      if (!(ins || inn)) { s.clk = h.clk; s.joyp = jp; w = s.fetch_slow(pc, dec_s); }
     }
     const int op = w & 0xFF, b1 = (w >> 8) & 0xFF, imm16 = (w >> 8) & 0xFFFF;
     const int key = op == 0xCB ? 256 + b1 : op;

@@ -82,10 +82,21 @@ def _policy_class():
             self.head = nn.Sequential(nn.Linear(flat, 512), nn.ReLU(), nn.Linear(512, num_actions))
 
         def forward(self, frames_u8):  # [B, 72, 80] uint8 shades
+            return self.forward_scaled(frames_u8.unsqueeze(1).to(self.head[0].weight.dtype) / 3.0)
+
+        def forward_scaled(self, x):  # [B, 1, 72, 80] shades / 3 in the weights' dtype
             # one channel: NCHW and NHWC are the same bytes; channels-last
             # keeps every conv in NHWC (no layout transposes around cuDNN)
-            x = frames_u8.unsqueeze(1).to(self.head[0].weight.dtype) / 3.0
-            return self.head(self.conv(x.contiguous(memory_format=torch.channels_last)))
+            x = x.contiguous(memory_format=torch.channels_last)
+            if not x.is_cuda:
+                return self.head(self.conv(x))
+            # on the GPU each Conv2d + bias + ReLU is one cuDNN call (the
+            # unfused module adds the bias and applies the ReLU as two more
+            # passes over every activation)
+            for conv in (self.conv[0], self.conv[2], self.conv[4]):
+                x = torch.ops.aten.cudnn_convolution_relu(x, conv.weight, conv.bias, conv.stride, conv.padding,
+                                                         conv.dilation, conv.groups)
+            return self.head(x.flatten(1))
 
     return PixelPolicy
 
@@ -108,7 +119,7 @@ class Rollout:
 def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 16384,
                 reset_cache=None, reset_mask: Callable[[int], Any] | None = None,
                 packed_out=None, step_events=None, host_out=None, instr_acc=None) -> Rollout:
-    """``steps`` env-steps of render -> unpack -> policy -> sample -> step.
+    """``steps`` env-steps of render -> policy -> sample -> step.
 
     ``reset_mask(k)`` (a CUDA bool/uint8 [N] or None) selects envs restored
     from ``reset_cache`` after step k. The policy runs in chunks of ``chunk``
@@ -127,14 +138,24 @@ def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 163
     n = backend.num_envs
     dev = torch.device("cuda", backend._ordinal)
     packed = packed_out if packed_out is not None else torch.empty((n, 72, 20), dtype=torch.uint8, device=dev)
+    # a bf16 policy reads the frames the render writes beside the packed
+    # bytes (shade / 3 in bf16: the same values as unpacking and dividing)
+    wdt = next(policy.parameters()).dtype
+    scaled = torch.empty((n, 1, 72, 80), dtype=wdt, device=dev) if wdt is torch.bfloat16 else None
     out = Rollout()
     with torch.no_grad():
         for k in range(steps):
-            backend.render_pixels_snapshot_packed_to_torch(packed)
+            if scaled is not None:
+                backend.render_pixels_snapshot_packed_scaled_to_torch(packed, scaled)
+            else:
+                backend.render_pixels_snapshot_packed_to_torch(packed)
             acts = torch.empty(n, dtype=torch.int32, device=dev)
             for lo in range(0, n, chunk):
                 hi = min(n, lo + chunk)
-                logits = policy(unpack_2bpp_u8(packed[lo:hi])).float()
+                if scaled is not None:
+                    logits = policy.forward_scaled(scaled[lo:hi]).float()
+                else:
+                    logits = policy(unpack_2bpp_u8(packed[lo:hi])).float()
                 acts[lo:hi] = torch.multinomial(torch.softmax(logits, dim=-1), 1, generator=generator)[:, 0].to(torch.int32)
             if host_out is not None:
                 host_out[0][k % 2].copy_(packed, non_blocking=True)

@@ -24,7 +24,7 @@
 extern "C" {
 #endif
 
-#define GBX_ABI_VERSION 4
+#define GBX_ABI_VERSION 5
 
 typedef enum {
   GBX_OK = 0,
@@ -185,6 +185,13 @@ int gbx_set_dispatch(gbx_env* env, int32_t dispatch);
  * render_pixels_snapshot_packed_to_torch (warp_vec.py:1293-1352) and
  * render_pixels_snapshot (:727-732). */
 int gbx_render_packed(gbx_env* env, uint8_t* out, int64_t base_offset, void* stream);
+/* gbx_render_packed plus, in the same pass, the policy input a consumer
+ * builds from the packed frame: every pixel as bf16 (shade / 3.0, rounded to
+ * nearest even as torch rounds float -> bf16), [n][72][80] into `scaled`
+ * (device, 16-byte aligned, n*5760*2 bytes). Replaces the consumer-side
+ * unpack of rl/packed_pixels.py:26-71 followed by the policy's frames / 3.0
+ * (the reference's rollouts run those as separate torch passes). */
+int gbx_render_packed_scaled(gbx_env* env, uint8_t* out, int64_t base_offset, void* scaled, void* stream);
 int gbx_render_shades(gbx_env* env, uint8_t* out, void* stream);
 
 /* Capture env env_idx into a device snapshot (ResetCache.from_backend,

@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     assert len(names) >= 20
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.gbx_abi_version() == L.ABI_VERSION == 4
+    assert lib.gbx_abi_version() == L.ABI_VERSION == 5
 
 
 def test_create_validates_before_touching_a_device():

@@ -369,9 +369,10 @@ def test_state_files_match_reference_on_gpu(name, tmp_path):
 
 
 def test_policy_rollout_with_resets_replays_on_oracle():
-    """Config-5 rollout shape: packed frames -> bf16 policy -> sampled actions
-    -> step_torch, with masked restores from a ResetCache; the recorded
-    actions and masks replayed on the oracle give the same state and frames."""
+    """Config-5 rollout shape: packed frames (and the policy's bf16 input from
+    the same render) -> bf16 policy -> sampled actions -> step_torch, with
+    masked restores from a ResetCache; the recorded actions and masks
+    replayed on the oracle give the same state and frames."""
     from gbxcule_b200 import ResetCache, rollout
 
     rom = roms.config5_rom()
@@ -388,13 +389,16 @@ def test_policy_rollout_with_resets_replays_on_oracle():
         gen = torch.Generator(device="cuda").manual_seed(11)
         masks = [torch.as_tensor(np.random.default_rng(60 + k).random(n) < 0.25, device="cuda") for k in range(4)]
         frames = []
-        orig = be.render_pixels_snapshot_packed_to_torch
+        orig = be.render_pixels_snapshot_packed_scaled_to_torch
 
-        def rec(out, base_offset_bytes=0):
-            orig(out, base_offset_bytes)
+        def rec(out, scaled, base_offset_bytes=0):
+            orig(out, scaled, base_offset_bytes)
             frames.append(out.clone())
+            # the policy's input: the packed frame unpacked, as bf16, / 3.0
+            want = rollout.unpack_2bpp_u8(out).unsqueeze(1).to(torch.bfloat16) / 3.0
+            assert torch.equal(scaled.view(torch.int16), want.view(torch.int16))
 
-        be.render_pixels_snapshot_packed_to_torch = rec
+        be.render_pixels_snapshot_packed_scaled_to_torch = rec
         ro = rollout.run_rollout(be, pol, 4, generator=gen, reset_cache=cache, reset_mask=lambda k: masks[k])
         for k in range(4):
             assert np.array_equal(frames[k].cpu().numpy(), o.render_packed()), f"policy input {k}"
@@ -437,3 +441,50 @@ def test_two_rank_slices_equal_one_batch():
         whole.close()
         for be in parts:
             be.close()
+
+
+def test_scaled_render_equals_unpacked_frames_over_three():
+    """gbx_render_packed_scaled: the packed bytes equal the plain packed
+    render, and the bf16 image equals unpack -> bf16 -> / 3.0 bit for bit,
+    at an offset into a larger packed buffer as well."""
+    from gbxcule_b200 import rollout
+
+    rom = roms.config2_rom()
+    n = 48
+    be = _backend(rom, n, 24, 8, render_pixels_packed=True)
+    try:
+        rng = np.random.default_rng(8)
+        for _ in range(7):  # past the ROM's VRAM set-up: tiles, window and sprites on screen
+            _step(be, roms.uniform_actions(rng, n))
+        plain = torch.empty((n, 72, 20), dtype=torch.uint8, device="cuda")
+        be.render_pixels_snapshot_packed_to_torch(plain)
+        big = torch.zeros(1440 * n + 4096, dtype=torch.uint8, device="cuda")
+        scaled = torch.full((n, 1, 72, 80), -1.0, dtype=torch.bfloat16, device="cuda")
+        be.render_pixels_snapshot_packed_scaled_to_torch(big, scaled, 1024)
+        torch.cuda.synchronize()
+        assert torch.equal(big[1024:1024 + 1440 * n].view(n, 72, 20), plain)
+        assert int(big[:1024].sum()) == 0 and int(big[1024 + 1440 * n:].sum()) == 0
+        want = rollout.unpack_2bpp_u8(plain).unsqueeze(1).to(torch.bfloat16) / 3.0
+        assert torch.equal(scaled.view(torch.int16), want.view(torch.int16))
+        assert len(torch.unique(want)) > 1
+        with pytest.raises(ValueError):
+            be.render_pixels_snapshot_packed_scaled_to_torch(None, scaled.float())
+    finally:
+        be.close()
+
+
+def test_fused_policy_matches_module_within_bf16_tolerance():
+    """The policy's GPU path (each Conv2d + bias + ReLU as one cuDNN call)
+    against the plain module on the same bf16 input: equal up to bf16
+    rounding (tolerance: 2 % of the largest logit + 0.02)."""
+    from gbxcule_b200 import rollout
+
+    pol = rollout.make_policy("cuda", seed=3)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    shades = torch.randint(0, 4, (512, 72, 80), generator=g, device="cuda", dtype=torch.uint8)
+    with torch.no_grad():
+        x = shades.unsqueeze(1).to(torch.bfloat16) / 3.0
+        fused = pol.forward_scaled(x).float()
+        plain = pol.head(pol.conv(x.contiguous(memory_format=torch.channels_last))).float()
+    tol = 0.02 * float(plain.abs().max()) + 0.02
+    assert float((fused - plain).abs().max()) <= tol
