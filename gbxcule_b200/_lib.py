@@ -75,7 +75,7 @@ def lib():
         "gbx_reset": ([P, P], c_int32),
         "gbx_step": ([P, P, c_int32, c_int32, P], c_int32),
         "gbx_render_packed": ([P, P, c_int64, P], c_int32),
-        "gbx_render_packed_scaled": ([P, P, c_int64, P, P], c_int32),
+        "gbx_render_packed_scaled": ([P, P, c_int64, P, c_int32, P], c_int32),
         "gbx_render_shades": ([P, P, P], c_int32),
         "gbx_snapshot_create": ([P, c_int32, P, E], c_int32),
         "gbx_snapshot_destroy": ([P], c_int32),

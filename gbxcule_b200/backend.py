@@ -324,13 +324,18 @@ class GbxVecCudaBackend:
         L.check(self._lib.gbx_render_packed(self._h, ctypes.c_void_p(out.data_ptr()), int(base_offset_bytes),
                                             self._stream()), "gbx_render_packed")
 
-    def render_pixels_snapshot_packed_scaled_to_torch(self, out, scaled, base_offset_bytes: int = 0) -> None:
+    def render_pixels_snapshot_packed_scaled_to_torch(self, out, scaled, base_offset_bytes: int = 0,
+                                                       layout: str = "rows") -> None:
         """``render_pixels_snapshot_packed_to_torch`` plus the policy input in
         the same launch: ``scaled`` (CUDA bf16, contiguous, >= N*72*80
         elements) receives every pixel as shade / 3.0 in bf16, the tensor a
         consumer gets from unpacking the packed bytes (rl/packed_pixels.py:26-71)
-        and dividing by 3.0. ``out`` may be None (the backend's own packed
-        buffer)."""
+        and dividing by 3.0, as [N, 72, 80] rows (``layout="rows"``) or 2x2
+        space-to-depth [N, 36, 40, 4] (``layout="s2d"``: pixel (y, x) at
+        (y//2, x//2, (y%2)*2 + x%2)). ``out`` may be None (the backend's own
+        packed buffer)."""
+        if layout not in ("rows", "s2d"):
+            raise ValueError(f"layout must be 'rows' or 's2d', got {layout!r}")
         if not self._initialized or self._h is None:
             raise RuntimeError("Backend not initialized. Call reset() first.")
         torch = self._torch()
@@ -354,7 +359,8 @@ class GbxVecCudaBackend:
         if self._force_lcdc_on_render:
             self._apply_lcdc_override()
         L.check(self._lib.gbx_render_packed_scaled(self._h, ptr, int(base_offset_bytes),
-                                                   ctypes.c_void_p(scaled.data_ptr()), self._stream()),
+                                                   ctypes.c_void_p(scaled.data_ptr()), int(layout == "s2d"),
+                                                   self._stream()),
                 "gbx_render_packed_scaled")
 
     def pixels_torch(self):

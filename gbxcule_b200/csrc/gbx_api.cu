@@ -23,7 +23,7 @@ int dispatch_override();
 cudaError_t launch_render_bg_env0(const DevState& st, uint8_t* out, cudaStream_t stream);
 void predecode_rom(const uint8_t* rom, int n, uint32_t* out);
 cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
-                          cudaStream_t stream, uint16_t* scaled, uint64_t scale_tab);
+                          cudaStream_t stream, uint16_t* scaled, uint64_t scale_tab, int s2d);
 cudaError_t launch_init(const DevState& st, cudaStream_t s, int sms);
 cudaError_t launch_snapshot(const DevState& st, const Snapshot& snap, int env, cudaStream_t s);
 cudaError_t launch_restore(const DevState& st, const Snapshot& snap, const uint8_t* mask, cudaStream_t s,
@@ -498,7 +498,7 @@ int gbx_render_packed(gbx_env* h, uint8_t* out, int64_t base_offset, void* strea
     base_offset = 0;
   }
   DeviceGuard g(h->cfg.device);
-  CK(launch_render(h->st, out, base_offset, true, S_(stream), nullptr, 0), "render kernel");
+  CK(launch_render(h->st, out, base_offset, true, S_(stream), nullptr, 0, 0), "render kernel");
   return GBX_OK;
 }
 
@@ -509,9 +509,11 @@ static uint16_t bf16_bits(float v) {
   return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
 }
 
-int gbx_render_packed_scaled(gbx_env* h, uint8_t* out, int64_t base_offset, void* scaled, void* stream) {
+int gbx_render_packed_scaled(gbx_env* h, uint8_t* out, int64_t base_offset, void* scaled, int32_t layout,
+                             void* stream) {
   RET(check_init(h));
   if (base_offset < 0) return fail(GBX_ERR_INVALID, "base_offset_bytes must be >= 0");
+  if (layout != 0 && layout != 1) return fail(GBX_ERR_INVALID, "layout must be 0 (rows) or 1 (space-to-depth), got %d", layout);
   if (!scaled) return fail(GBX_ERR_INVALID, "scaled output is null");
   if (reinterpret_cast<uintptr_t>(scaled) & 15) return fail(GBX_ERR_INVALID, "scaled output must be 16-byte aligned");
   if (!out) {
@@ -522,7 +524,7 @@ int gbx_render_packed_scaled(gbx_env* h, uint8_t* out, int64_t base_offset, void
   uint64_t tab = 0;
   for (int v = 0; v < 4; v++) tab |= (uint64_t)bf16_bits((float)v / 3.0f) << (16 * v);
   DeviceGuard g(h->cfg.device);
-  CK(launch_render(h->st, out, base_offset, true, S_(stream), static_cast<uint16_t*>(scaled), tab),
+  CK(launch_render(h->st, out, base_offset, true, S_(stream), static_cast<uint16_t*>(scaled), tab, layout),
      "render kernel");
   return GBX_OK;
 }
@@ -534,7 +536,7 @@ int gbx_render_shades(gbx_env* h, uint8_t* out, void* stream) {
     out = h->pix;
   }
   DeviceGuard g(h->cfg.device);
-  CK(launch_render(h->st, out, 0, false, S_(stream), nullptr, 0), "render kernel");
+  CK(launch_render(h->st, out, 0, false, S_(stream), nullptr, 0, 0), "render kernel");
   return GBX_OK;
 }
 

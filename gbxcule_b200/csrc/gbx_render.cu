@@ -31,12 +31,15 @@ constexpr int OUT_ROWS = 72;
 
 // scaled (packed renders only, may be null): the same image as the policy
 // input a consumer builds from the packed bytes (unpack, to bf16, / 3.0), one
-// bf16 per pixel [N][72][80]; scale_tab holds the bf16 bits of shade / 3 for
-// shades 0..3 (16 bits each).
+// bf16 per output pixel, as [N][72][80] (s2d = 0) or space-to-depth
+// [N][36][40][4] (s2d = 1: pixel (oy, ox) at (oy/2, ox/2, (oy&1)*2 + (ox&1)));
+// scale_tab holds
+// the bf16 bits of shade / 3 for shades 0..3 (16 bits each).
 template <bool PACKED>
 __global__ void __launch_bounds__(RENDER_THREADS) render_kernel(DevState st, uint8_t* __restrict__ out,
                                                                int64_t base_offset, int vec,
-                                                               uint16_t* __restrict__ scaled, uint64_t scale_tab) {
+                                                               uint16_t* __restrict__ scaled, uint64_t scale_tab,
+                                                               int s2d) {
   constexpr int BPR = PACKED ? 20 : 80;  // output bytes per row
   constexpr int ENV_BYTES = OUT_ROWS * BPR;
   __shared__ __align__(16) uint8_t vram[0x2000];
@@ -136,13 +139,19 @@ __global__ void __launch_bounds__(RENDER_THREADS) render_kernel(DevState st, uin
       packed |= (shade & 3) << (2 * k);
     }
     img[i] = (uint8_t)packed;
-    if (PACKED && scaled) {  // four pixels = one 8-byte store, consecutive threads adjacent
-      uint2 v;
-      v.x = (uint32_t)((scale_tab >> (16 * (packed & 3))) & 0xFFFF) |
-            ((uint32_t)((scale_tab >> (16 * ((packed >> 2) & 3))) & 0xFFFF) << 16);
-      v.y = (uint32_t)((scale_tab >> (16 * ((packed >> 4) & 3))) & 0xFFFF) |
-            ((uint32_t)((scale_tab >> (16 * ((packed >> 6) & 3))) & 0xFFFF) << 16);
-      reinterpret_cast<uint2*>(scaled + (size_t)env * (OUT_ROWS * 80))[i] = v;
+    if (PACKED && scaled) {
+      const uint32_t p0 = (uint32_t)((scale_tab >> (16 * (packed & 3))) & 0xFFFF);
+      const uint32_t p1 = (uint32_t)((scale_tab >> (16 * ((packed >> 2) & 3))) & 0xFFFF);
+      const uint32_t p2 = (uint32_t)((scale_tab >> (16 * ((packed >> 4) & 3))) & 0xFFFF);
+      const uint32_t p3 = (uint32_t)((scale_tab >> (16 * ((packed >> 6) & 3))) & 0xFFFF);
+      uint16_t* e = scaled + (size_t)env * (OUT_ROWS * 80);
+      if (!s2d) {  // four pixels = one 8-byte store, consecutive threads adjacent
+        reinterpret_cast<uint2*>(e)[i] = make_uint2(p0 | (p1 << 16), p2 | (p3 << 16));
+      } else {     // pixels (oy, 4ob..4ob+3) -> cells (oy/2, 2ob) and (oy/2, 2ob+1), channels (oy&1)*2 + 0/1
+        uint32_t* c = reinterpret_cast<uint32_t*>(e + (((oy >> 1) * 40 + 2 * ob) * 4 + (oy & 1) * 2));
+        c[0] = p0 | (p1 << 16);
+        c[2] = p2 | (p3 << 16);
+      }
     }
   }
   __syncthreads();
@@ -235,13 +244,13 @@ cudaError_t launch_render_bg_env0(const DevState& st, uint8_t* out, cudaStream_t
 }
 
 cudaError_t launch_render(const DevState& st, uint8_t* out, int64_t base_offset, bool packed,
-                          cudaStream_t stream, uint16_t* scaled, uint64_t scale_tab) {
+                          cudaStream_t stream, uint16_t* scaled, uint64_t scale_tab, int s2d) {
   // every env image starts 16-byte aligned when the buffer start is (1440 and 5760 are multiples of 16)
   const int vec = ((reinterpret_cast<uintptr_t>(out) + (uintptr_t)base_offset) & 15) == 0;
   if (packed)
-    render_kernel<true><<<st.n, RENDER_THREADS, 0, stream>>>(st, out, base_offset, vec, scaled, scale_tab);
+    render_kernel<true><<<st.n, RENDER_THREADS, 0, stream>>>(st, out, base_offset, vec, scaled, scale_tab, s2d);
   else
-    render_kernel<false><<<st.n, RENDER_THREADS, 0, stream>>>(st, out, base_offset, vec, nullptr, 0);
+    render_kernel<false><<<st.n, RENDER_THREADS, 0, stream>>>(st, out, base_offset, vec, nullptr, 0, 0);
   return cudaGetLastError();
 }
 

@@ -66,6 +66,22 @@ def pack_2bpp_u8(pixels) -> Any:
     return q[..., 0] | (q[..., 1] << 2) | (q[..., 2] << 4) | (q[..., 3] << 6)
 
 
+def s2d_frames(x) -> Any:
+    """[B, 1, 72, 80] -> [B, 36, 40, 4]: 2x2 space-to-depth, pixel (y, x) at
+    (y // 2, x // 2, (y % 2) * 2 + x % 2) (the layout of
+    ``render_pixels_snapshot_packed_scaled_to_torch(..., layout="s2d")``)."""
+    b = x.shape[0]
+    return x.reshape(b, 36, 2, 40, 2).permute(0, 1, 3, 2, 4).reshape(b, 36, 40, 4)
+
+
+def s2d_weight(w) -> Any:
+    """Conv weight [O, 1, 4, 4] of a stride-2 convolution -> [O, 4, 2, 2] of
+    the stride-1 convolution over the 2x2 space-to-depth input that computes
+    the same sums: tap (2a + dy, 2b + dx) moves to channel 2 dy + dx at (a, b)."""
+    o = w.shape[0]
+    return w.reshape(o, 2, 2, 2, 2).permute(0, 2, 4, 1, 3).reshape(o, 4, 2, 2)
+
+
 def _policy_class():
     import torch
     from torch import nn
@@ -94,6 +110,24 @@ def _policy_class():
             # unfused module adds the bias and applies the ReLU as two more
             # passes over every activation)
             for conv in (self.conv[0], self.conv[2], self.conv[4]):
+                x = torch.ops.aten.cudnn_convolution_relu(x, conv.weight, conv.bias, conv.stride, conv.padding,
+                                                         conv.dilation, conv.groups)
+            return self.head(x.flatten(1))
+
+        def forward_s2d(self, x):  # [B, 36, 40, 4] shades / 3, 2x2 space-to-depth (cell, then (y%2)*2 + x%2)
+            # Conv(1->32, k4, s2) over the 72x80 frame is the same sum as a
+            # stride-1 k2 convolution over the 4 channels of its 2x2
+            # space-to-depth (kernel tap (2a+dy, 2b+dx) -> channel 2dy+dx at
+            # (a, b)), which cuDNN runs as an implicit GEMM instead of its
+            # one-channel direct engine. GPU only.
+            c1 = self.conv[0]
+            w = getattr(self, "_w_s2d", None)
+            if w is None or w.dtype != c1.weight.dtype or w.device != c1.weight.device:
+                w = s2d_weight(c1.weight).contiguous(memory_format=torch.channels_last)
+                self._w_s2d = w
+            x = x.permute(0, 3, 1, 2)  # NHWC bytes seen as an NCHW tensor in channels-last order
+            x = torch.ops.aten.cudnn_convolution_relu(x, w, c1.bias, (1, 1), (0, 0), (1, 1), 1)
+            for conv in (self.conv[2], self.conv[4]):
                 x = torch.ops.aten.cudnn_convolution_relu(x, conv.weight, conv.bias, conv.stride, conv.padding,
                                                          conv.dilation, conv.groups)
             return self.head(x.flatten(1))
@@ -139,21 +173,22 @@ def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 163
     dev = torch.device("cuda", backend._ordinal)
     packed = packed_out if packed_out is not None else torch.empty((n, 72, 20), dtype=torch.uint8, device=dev)
     # a bf16 policy reads the frames the render writes beside the packed
-    # bytes (shade / 3 in bf16: the same values as unpacking and dividing)
+    # bytes (shade / 3 in bf16: the same values as unpacking and dividing),
+    # in the 2x2 space-to-depth layout of its first convolution
     wdt = next(policy.parameters()).dtype
-    scaled = torch.empty((n, 1, 72, 80), dtype=wdt, device=dev) if wdt is torch.bfloat16 else None
+    scaled = torch.empty((n, 36, 40, 4), dtype=wdt, device=dev) if wdt is torch.bfloat16 else None
     out = Rollout()
     with torch.no_grad():
         for k in range(steps):
             if scaled is not None:
-                backend.render_pixels_snapshot_packed_scaled_to_torch(packed, scaled)
+                backend.render_pixels_snapshot_packed_scaled_to_torch(packed, scaled, layout="s2d")
             else:
                 backend.render_pixels_snapshot_packed_to_torch(packed)
             acts = torch.empty(n, dtype=torch.int32, device=dev)
             for lo in range(0, n, chunk):
                 hi = min(n, lo + chunk)
                 if scaled is not None:
-                    logits = policy.forward_scaled(scaled[lo:hi]).float()
+                    logits = policy.forward_s2d(scaled[lo:hi]).float()
                 else:
                     logits = policy(unpack_2bpp_u8(packed[lo:hi])).float()
                 acts[lo:hi] = torch.multinomial(torch.softmax(logits, dim=-1), 1, generator=generator)[:, 0].to(torch.int32)

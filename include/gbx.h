@@ -187,11 +187,15 @@ int gbx_set_dispatch(gbx_env* env, int32_t dispatch);
 int gbx_render_packed(gbx_env* env, uint8_t* out, int64_t base_offset, void* stream);
 /* gbx_render_packed plus, in the same pass, the policy input a consumer
  * builds from the packed frame: every pixel as bf16 (shade / 3.0, rounded to
- * nearest even as torch rounds float -> bf16), [n][72][80] into `scaled`
- * (device, 16-byte aligned, n*5760*2 bytes). Replaces the consumer-side
- * unpack of rl/packed_pixels.py:26-71 followed by the policy's frames / 3.0
- * (the reference's rollouts run those as separate torch passes). */
-int gbx_render_packed_scaled(gbx_env* env, uint8_t* out, int64_t base_offset, void* scaled, void* stream);
+ * nearest even as torch rounds float -> bf16) into `scaled` (device, 16-byte
+ * aligned, n*5760*2 bytes), laid out [n][72][80] (layout 0) or as 2x2
+ * space-to-depth [n][36][40][4] (layout 1: pixel (y, x) at (y/2, x/2,
+ * (y&1)*2 + (x&1)), the input of a stride-2 convolution rewritten as a
+ * stride-1 one over 4 channels). Replaces the consumer-side unpack of
+ * rl/packed_pixels.py:26-71 followed by the policy's frames / 3.0 (the
+ * reference's rollouts run those as separate torch passes). */
+int gbx_render_packed_scaled(gbx_env* env, uint8_t* out, int64_t base_offset, void* scaled, int32_t layout,
+                             void* stream);
 int gbx_render_shades(gbx_env* env, uint8_t* out, void* stream);
 
 /* Capture env env_idx into a device snapshot (ResetCache.from_backend,

@@ -391,12 +391,14 @@ def test_policy_rollout_with_resets_replays_on_oracle():
         frames = []
         orig = be.render_pixels_snapshot_packed_scaled_to_torch
 
-        def rec(out, scaled, base_offset_bytes=0):
-            orig(out, scaled, base_offset_bytes)
+        def rec(out, scaled, base_offset_bytes=0, layout="rows"):
+            orig(out, scaled, base_offset_bytes, layout)
             frames.append(out.clone())
             # the policy's input: the packed frame unpacked, as bf16, / 3.0
             want = rollout.unpack_2bpp_u8(out).unsqueeze(1).to(torch.bfloat16) / 3.0
-            assert torch.equal(scaled.view(torch.int16), want.view(torch.int16))
+            if layout == "s2d":
+                want = rollout.s2d_frames(want)
+            assert torch.equal(scaled.view(torch.int16), want.reshape(scaled.shape).view(torch.int16))
 
         be.render_pixels_snapshot_packed_scaled_to_torch = rec
         ro = rollout.run_rollout(be, pol, 4, generator=gen, reset_cache=cache, reset_mask=lambda k: masks[k])
@@ -467,6 +469,11 @@ def test_scaled_render_equals_unpacked_frames_over_three():
         want = rollout.unpack_2bpp_u8(plain).unsqueeze(1).to(torch.bfloat16) / 3.0
         assert torch.equal(scaled.view(torch.int16), want.view(torch.int16))
         assert len(torch.unique(want)) > 1
+        s2d = torch.empty((n, 36, 40, 4), dtype=torch.bfloat16, device="cuda")
+        be.render_pixels_snapshot_packed_scaled_to_torch(None, s2d, layout="s2d")
+        torch.cuda.synchronize()
+        assert torch.equal(s2d.view(torch.int16), rollout.s2d_frames(want).view(torch.int16))
+        assert torch.equal(be.pixels_packed_torch(), plain)
         with pytest.raises(ValueError):
             be.render_pixels_snapshot_packed_scaled_to_torch(None, scaled.float())
     finally:
@@ -474,9 +481,10 @@ def test_scaled_render_equals_unpacked_frames_over_three():
 
 
 def test_fused_policy_matches_module_within_bf16_tolerance():
-    """The policy's GPU path (each Conv2d + bias + ReLU as one cuDNN call)
-    against the plain module on the same bf16 input: equal up to bf16
-    rounding (tolerance: 2 % of the largest logit + 0.02)."""
+    """The policy's GPU paths (each Conv2d + bias + ReLU as one cuDNN call;
+    the first convolution also over the space-to-depth frame) against the
+    plain module on the same bf16 input: equal up to bf16 rounding
+    (tolerance: 2 % of the largest logit + 0.02)."""
     from gbxcule_b200 import rollout
 
     pol = rollout.make_policy("cuda", seed=3)
@@ -486,5 +494,7 @@ def test_fused_policy_matches_module_within_bf16_tolerance():
         x = shades.unsqueeze(1).to(torch.bfloat16) / 3.0
         fused = pol.forward_scaled(x).float()
         plain = pol.head(pol.conv(x.contiguous(memory_format=torch.channels_last))).float()
+        s2d = pol.forward_s2d(rollout.s2d_frames(x)).float()
     tol = 0.02 * float(plain.abs().max()) + 0.02
     assert float((fused - plain).abs().max()) <= tol
+    assert float((s2d - plain).abs().max()) <= tol

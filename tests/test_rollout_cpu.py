@@ -27,3 +27,24 @@ def test_policy_shape():
     pol = rollout.make_policy("cpu", dtype=torch.float32)
     logits = pol(torch.randint(0, 4, (3, 72, 80), dtype=torch.uint8))
     assert logits.shape == (3, 9)
+
+
+def test_space_to_depth_conv_computes_the_stride_two_conv():
+    """Conv(1->32, k4, s2) over the frame equals the k2 stride-1 convolution
+    of its 2x2 space-to-depth with the rearranged weight (fp32, CPU)."""
+    import torch
+    import torch.nn.functional as F
+
+    from gbxcule_b200 import rollout
+
+    g = torch.Generator().manual_seed(7)
+    x = torch.randint(0, 4, (3, 1, 72, 80), generator=g).float() / 3.0
+    w = torch.randn(32, 1, 4, 4, generator=g)
+    b = torch.randn(32, generator=g)
+    want = F.conv2d(x, w, b, stride=2)
+    s = rollout.s2d_frames(x)
+    assert s.shape == (3, 36, 40, 4)
+    assert torch.equal(s[:, 5, 7, 3], x[:, 0, 11, 15]) and torch.equal(s[:, 5, 7, 2], x[:, 0, 11, 14])
+    got = F.conv2d(s.permute(0, 3, 1, 2), rollout.s2d_weight(w), b, stride=1)
+    assert got.shape == want.shape == (3, 32, 35, 39)
+    assert torch.allclose(got, want, atol=1e-5)
