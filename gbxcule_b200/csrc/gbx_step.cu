@@ -1838,14 +1838,6 @@ static cudaError_t launch_t(const DevState& st, const uint32_t* pre, const int32
   cudaError_t e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT, DBG, UNI>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
-  // GBX_SMEM_CARVEOUT (percent of the unified L1/shared storage given to
-  // shared memory, experiments): unset = the driver's choice
-  const int carve = env_int("GBX_SMEM_CARVEOUT", -1);
-  if (carve >= 0) {
-    e = cudaFuncSetAttribute(gb_step_kernel<MBC, MAXT, DBG, UNI>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             carve > 100 ? 100 : carve);
-    if (e != cudaSuccess) return e;
-  }
   gb_step_kernel<MBC, MAXT, DBG, UNI><<<blocks, threads, sm, stream>>>(st, pre, actions, frames, release, stage,
                                                                       K, pre_s_words, dbg);
   return cudaGetLastError();
