@@ -121,10 +121,13 @@ def _policy_class():
             # (a, b)), which cuDNN runs as an implicit GEMM instead of its
             # one-channel direct engine. GPU only.
             c1 = self.conv[0]
-            w = getattr(self, "_w_s2d", None)
-            if w is None or w.dtype != c1.weight.dtype or w.device != c1.weight.device:
-                w = s2d_weight(c1.weight).contiguous(memory_format=torch.channels_last)
-                self._w_s2d = w
+            # rearranged weight, rebuilt whenever the weight changes (an
+            # optimizer step updates it in place and bumps its version)
+            key = (c1.weight.data_ptr(), c1.weight._version, c1.weight.dtype)
+            if getattr(self, "_w_s2d_key", None) != key:
+                self._w_s2d = s2d_weight(c1.weight.detach()).contiguous(memory_format=torch.channels_last)
+                self._w_s2d_key = key
+            w = self._w_s2d
             x = x.permute(0, 3, 1, 2)  # NHWC bytes seen as an NCHW tensor in channels-last order
             x = torch.ops.aten.cudnn_convolution_relu(x, w, c1.bias, (1, 1), (0, 0), (1, 1), 1)
             for conv in (self.conv[2], self.conv[4]):

@@ -48,3 +48,18 @@ def test_space_to_depth_conv_computes_the_stride_two_conv():
     got = F.conv2d(s.permute(0, 3, 1, 2), rollout.s2d_weight(w), b, stride=1)
     assert got.shape == want.shape == (3, 32, 35, 39)
     assert torch.allclose(got, want, atol=1e-5)
+
+
+def test_s2d_weight_cache_follows_in_place_updates():
+    """The space-to-depth weight the policy caches is rebuilt after an in-place
+    update of the first convolution's weight (an optimizer step)."""
+    import torch
+
+    from gbxcule_b200 import rollout
+
+    pol = rollout.make_policy("cpu", dtype=torch.float32)
+    c1 = pol.conv[0]
+    key0 = (c1.weight.data_ptr(), c1.weight._version, c1.weight.dtype)
+    with torch.no_grad():
+        c1.weight.mul_(2.0)
+    assert (c1.weight.data_ptr(), c1.weight._version, c1.weight.dtype) != key0
