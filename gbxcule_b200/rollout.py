@@ -112,7 +112,29 @@ def _policy_class():
             for conv in (self.conv[0], self.conv[2], self.conv[4]):
                 x = torch.ops.aten.cudnn_convolution_relu(x, conv.weight, conv.bias, conv.stride, conv.padding,
                                                          conv.dilation, conv.groups)
-            return self.head(x.flatten(1))
+            return self._head_nhwc(x)
+
+        def _cached(self, name, src, make):
+            # derived weight, rebuilt whenever its source changes (an optimizer
+            # step updates the source in place and bumps its version)
+            key = (src.data_ptr(), src._version, src.dtype)
+            if getattr(self, name + "_key", None) != key:
+                setattr(self, name, make(src.detach()))
+                setattr(self, name + "_key", key)
+            return getattr(self, name)
+
+        def _head_nhwc(self, x):
+            # x: the last convolution's output, channels-last. Its features are
+            # read in NHWC order (a view, no copy) against the first linear
+            # layer's weight with its columns permuted from NCHW to NHWC order:
+            # the same sum as flattening NCHW, without the strided copy.
+            b, c, hh, ww = x.shape
+            lin1, lin2 = self.head[0], self.head[2]
+            w1 = self._cached("_w1_nhwc", lin1.weight,
+                              lambda w: w.reshape(w.shape[0], c, hh, ww).permute(0, 2, 3, 1).reshape(w.shape[0], -1)
+                              .contiguous())
+            h = torch.relu(torch.nn.functional.linear(x.permute(0, 2, 3, 1).reshape(b, -1), w1, lin1.bias))
+            return torch.nn.functional.linear(h, lin2.weight, lin2.bias)
 
         def forward_s2d(self, x):  # [B, 36, 40, 4] shades / 3, 2x2 space-to-depth (cell, then (y%2)*2 + x%2)
             # Conv(1->32, k4, s2) over the 72x80 frame is the same sum as a
@@ -121,19 +143,14 @@ def _policy_class():
             # (a, b)), which cuDNN runs as an implicit GEMM instead of its
             # one-channel direct engine. GPU only.
             c1 = self.conv[0]
-            # rearranged weight, rebuilt whenever the weight changes (an
-            # optimizer step updates it in place and bumps its version)
-            key = (c1.weight.data_ptr(), c1.weight._version, c1.weight.dtype)
-            if getattr(self, "_w_s2d_key", None) != key:
-                self._w_s2d = s2d_weight(c1.weight.detach()).contiguous(memory_format=torch.channels_last)
-                self._w_s2d_key = key
-            w = self._w_s2d
+            w = self._cached("_w_s2d", c1.weight,
+                             lambda w: s2d_weight(w).contiguous(memory_format=torch.channels_last))
             x = x.permute(0, 3, 1, 2)  # NHWC bytes seen as an NCHW tensor in channels-last order
             x = torch.ops.aten.cudnn_convolution_relu(x, w, c1.bias, (1, 1), (0, 0), (1, 1), 1)
             for conv in (self.conv[2], self.conv[4]):
                 x = torch.ops.aten.cudnn_convolution_relu(x, conv.weight, conv.bias, conv.stride, conv.padding,
                                                          conv.dilation, conv.groups)
-            return self.head(x.flatten(1))
+            return self._head_nhwc(x)
 
     return PixelPolicy
 

@@ -59,7 +59,23 @@ def test_s2d_weight_cache_follows_in_place_updates():
 
     pol = rollout.make_policy("cpu", dtype=torch.float32)
     c1 = pol.conv[0]
-    key0 = (c1.weight.data_ptr(), c1.weight._version, c1.weight.dtype)
+    key0 = (c1.weight.data_ptr(), c1.weight._version, c1.weight.dtype)  # the cache key of _cached
     with torch.no_grad():
         c1.weight.mul_(2.0)
     assert (c1.weight.data_ptr(), c1.weight._version, c1.weight.dtype) != key0
+
+
+def test_nhwc_head_equals_the_module_head():
+    """The policy head read in NHWC feature order with the permuted first-layer
+    weight computes the module's NCHW-flatten head (fp32, CPU)."""
+    import torch
+
+    from gbxcule_b200 import rollout
+
+    pol = rollout.make_policy("cpu", dtype=torch.float32)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(4, 64, 15, 17, generator=g).contiguous(memory_format=torch.channels_last)
+    with torch.no_grad():
+        want = pol.head(x.flatten(1))
+        got = pol._head_nhwc(x)
+    assert torch.allclose(got, want, atol=1e-5, rtol=1e-5)
