@@ -128,8 +128,10 @@ __host__ __device__ constexpr DecodeTable make_table() {
   return t;
 }
 __constant__ DecodeTable c_decode = make_table();
-// descriptors of the uniform interpreter (gbx_udesc.h), staged in shared memory
+// descriptors and rotate table of the uniform interpreter (gbx_udesc.h),
+// staged in shared memory
 __constant__ UDescTable c_udesc = make_udesc_table();
+__constant__ RotTable c_rot = make_rot_table();
 
 // Host: pre-decode a ROM image (every byte offset as an instruction start).
 void predecode_rom(const uint8_t* rom, int n, uint32_t* out) {
@@ -1007,8 +1009,8 @@ template <int MBC>
 __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int& ninstr, int& win_hi,
                                              int& bankN_off, int& cram_off, const uint32_t* rom_s,
                                              const uint32_t* __restrict__ rom_g, int pre_s_words,
-                                             const uint8_t* dec_s, const uint4* ud_s, int frames_to_run,
-                                             unsigned alive) {
+                                             const uint8_t* dec_s, const uint4* ud_s, const uint16_t* rot_s,
+                                             int frames_to_run, unsigned alive) {
   uint8_t* const mem = s.mem;
   uint8_t* const cram = s.cart_ram;
   // Byte accesses: VRAM, WRAM, HRAM and the mapped cart-RAM bank inline, JOYP
@@ -1130,14 +1132,9 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
     const int lop = (vx >> UV_LOP) & 3;
     const int la = P & Q, lo = P | Q;
     const int lres = lop == UL_AND ? la : lop == UL_OR ? lo : (lo ^ la);
-    // ---- rotate / shift / swap ----
-    const int cf = (F >> 4) & 1;
-    const int z3 = (x & 1) | (cf << 1) | ((x >> 7) << 2);  // bit0, carry, bit7, 0
-    const int inb = (z3 >> ((vx >> UV_RIN) & 3)) & 1;
-    const bool left = fa & UF_ROT_LEFT;
-    int rres = left ? (((x << 1) | inb) & 0xFF) : ((x >> 1) | (inb << 7));
-    if (fa & UF_SWAP) rres = ((x << 4) | (x >> 4)) & 0xFF;
-    const int rc = left ? (x >> 7) : (x & 1);
+    // ---- rotate / shift / swap: one lookup (kind, carry in, x) ----
+    const uint32_t rv = rot_s[q1.z | ((F & 0x10) << 4) | x];
+    const int rres = rv & 0xFF, rc = rv >> 8;
     // ---- 8-bit result and flags ----
     const int unit = (vx >> UV_UNIT) & 3;
     const int r8 = unit == UU_PASS ? x : unit == UU_ADD ? (S & 0xFF) : unit == UU_LOGIC ? lres : rres;
@@ -1246,7 +1243,7 @@ __device__ __forceinline__ void uniform_loop(Emu<MBC>& s, Hot& h, bool run, int&
 // per-family switch: for full warps of envs at different PCs.
 // Shared memory, switch: pre-decoded words of ROM offsets [0, P) | boot ROM |
 // family table. Uniform: raw ROM bytes [0, P + 16) | boot ROM | family table
-// | descriptor table. P = staged ROM offsets (pre_s_words).
+// | descriptor table | rotate table. P = staged ROM offsets (pre_s_words).
 __host__ __device__ constexpr size_t rom_smem_bytes(int P, bool uni) {
   return uni ? (((size_t)P + 16 + 15) & ~(size_t)15) : (size_t)P * 4;
 }
@@ -1261,6 +1258,7 @@ __global__ void __launch_bounds__(MAXT, 1)
   uint8_t* boot_s = smem + rom_smem_bytes(pre_s_words, UNI);
   uint8_t* dec_s = boot_s + 256;
   uint4* ud_s = reinterpret_cast<uint4*>(smem + udesc_smem_offset(pre_s_words));
+  uint16_t* rot_s = reinterpret_cast<uint16_t*>(smem + udesc_smem_offset(pre_s_words) + sizeof(UDescTable));
   {
     const uint4* src = UNI ? reinterpret_cast<const uint4*>(st.rom) : reinterpret_cast<const uint4*>(pre_g);
     uint4* dst = reinterpret_cast<uint4*>(pre_s);
@@ -1273,6 +1271,9 @@ __global__ void __launch_bounds__(MAXT, 1)
     if (UNI) {
       const uint4* ud = reinterpret_cast<const uint4*>(c_udesc.d);
       for (int k = threadIdx.x; k < UDESC_KEYS * 2; k += blockDim.x) ud_s[k] = ud[k];
+      const uint4* rt = reinterpret_cast<const uint4*>(c_rot.v);
+      uint4* rd = reinterpret_cast<uint4*>(rot_s);
+      for (int k = threadIdx.x; k < (int)(sizeof(RotTable) / 16); k += blockDim.x) rd[k] = rt[k];
     }
   }
   __syncthreads();
@@ -1421,7 +1422,8 @@ __global__ void __launch_bounds__(MAXT, 1)
       if (e < st.n) alive |= 1u << l;
     }
     uniform_loop<MBC>(s, h, run, ninstr, win_hi, bankN_off, cram_off, pre_s,
-                      reinterpret_cast<const uint32_t*>(st.rom), pre_s_words, dec_s, ud_s, frames_to_run, alive);
+                      reinterpret_cast<const uint32_t*>(st.rom), pre_s_words, dec_s, ud_s, rot_s, frames_to_run,
+                      alive);
   } else while (run) {
     // ---- fetch + decode ----
     const int pc = h.pc;
@@ -1865,7 +1867,8 @@ static cudaError_t launch_mbc(const DevState& st, const uint32_t* pre, const int
   if (uniform)  // one instantiation: the 64-register bound fits every block size
     return launch_t<MBC, 1024, false, true>(st, pre, actions, frames, release, stage, stream, K, threads,
                                             blocks, rom_words,
-                                            udesc_smem_offset(rom_words) + sizeof(UDescTable), dbg);
+                                            udesc_smem_offset(rom_words) + sizeof(UDescTable) + sizeof(RotTable),
+                                            dbg);
   if (threads <= 256)
     return launch_t<MBC, 256, false>(st, pre, actions, frames, release, stage, stream, K, threads, blocks,
                                      rom_words, sm, dbg);

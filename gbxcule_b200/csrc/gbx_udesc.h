@@ -15,7 +15,7 @@
 //                     the pushes; up to two bytes read at ea, ea + 1
 //   units     adder L + R (+carry) with 8- or 16-bit half/full carry taps;
 //             logic (AND / OR / XOR of A-or-x with x-or-constant);
-//             rotate/shift/swap of x
+//             rotate/shift/swap of x (one lookup in a 4096-entry table)
 //   results   8-bit register, 16-bit pair (BC DE HL SP AF), memory (one byte
 //             at ea or a 16-bit value as two bytes), flags by keep / computed
 //             / set / xor masks, SP += 0 / -2 / +2, PC from the sequential
@@ -42,7 +42,7 @@ enum UFlag : uint32_t {
   UF_EA_SP = 1u << 0, UF_EA_IMM8 = 1u << 1, UF_EA_IMM16 = 1u << 2, UF_EA_FF = 1u << 3, UF_EA_DEC = 1u << 4,
   UF_RD1 = 1u << 5, UF_RD2 = 1u << 6, UF_X_MEM = 1u << 7, UF_X_IMM = 1u << 8, UF_P_SP = 1u << 9,
   UF_P_AF = 1u << 10, UF_SUB = 1u << 11, UF_CIN = 1u << 12, UF_WIDE = 1u << 13, UF_SPECIAL = 1u << 14,
-  UF_R16_POP = 1u << 15, UF_LOFIRST = 1u << 16, UF_ROT_LEFT = 1u << 17, UF_SWAP = 1u << 18, UF_D8 = 1u << 19,
+  UF_R16_POP = 1u << 15, UF_LOFIRST = 1u << 16, UF_D8 = 1u << 19,
   UF_D8_HI = 1u << 20, UF_LX = 1u << 21, UF_QK = 1u << 22
 };
 constexpr int UF_SUB_BIT = 11, UF_EA_DEC_BIT = 4;
@@ -56,7 +56,6 @@ constexpr int UV_UNIT = 16;    // 2 bits
 constexpr int UV_LOP = 18;     // 2 bits
 constexpr int UV_LSEL = 20;    // 2 bits
 constexpr int UV_RSEL = 22;    // 2 bits
-constexpr int UV_RIN = 24;     // 2 bits
 constexpr int UV_TSEL = 26;    // 3 bits
 constexpr int UV_NW = 29;      // 2 bits
 // q1.y: [7:0] condition flag mask, [15:8] value that flag must have, then
@@ -68,7 +67,6 @@ enum UUnit { UU_PASS = 0, UU_ADD = 1, UU_LOGIC = 2, UU_ROT = 3 };
 enum ULop { UL_AND = 0, UL_OR = 1, UL_XOR = 2 };
 enum ULsel { ULS_A = 0, ULS_X = 1, ULS_EA = 2, ULS_P16 = 3 };
 enum URsel { URS_X = 0, URS_K = 1, URS_P16 = 2, URS_E8 = 3 };
-enum URin { URI_BIT0 = 0, URI_C = 1, URI_BIT7 = 2, URI_ZERO = 3 };
 enum UTsel { UT_SEQ = 0, UT_IMM16 = 1, UT_JR = 2, UT_EA = 3, UT_V16 = 4, UT_K = 5 };
 enum UD16 { UD_NONE = 0, UD_BC = 1, UD_DE = 2, UD_HL = 3, UD_SP = 4, UD_AF = 5 };
 enum UVsrc { UVS_P16 = 0, UVS_PCN = 1, UVS_SP = 2 };
@@ -80,7 +78,7 @@ struct UDesc {
 struct UDescB {  // builder
   uint32_t xsel = PS_ZERO, psel = PS_ZERO, easel = PS_ZERO, k16 = 0, flags = 0;
   uint32_t keep = 0xF0, comp = 0, set = 0, xr = 0;
-  uint32_t len = 1, cnt = 1, ct = 1, d8pos = 0, unit = UU_PASS, lop = 0, lsel = 0, rsel = 0, rin = 0, tsel = 0,
+  uint32_t len = 1, cnt = 1, ct = 1, d8pos = 0, unit = UU_PASS, lop = 0, lsel = 0, rsel = 0, rkind = 0, tsel = 0,
            nw = 0;
   uint32_t cmask = 0, cval = 0, d16 = 0, vsrc = 0, spd = 0;
 
@@ -130,10 +128,7 @@ struct UDescB {  // builder
   // rotate / shift / swap kind of x (bitops.py): RLC RRC RL RR SLA SRA SWAP SRL
   __host__ __device__ constexpr void rot(int kind) {
     unit = UU_ROT;
-    if (kind == 6) { flags |= UF_SWAP; return; }
-    if (kind == 0 || kind == 2 || kind == 4) flags |= UF_ROT_LEFT;
-    rin = kind == 0 ? URI_BIT7 : kind == 1 ? URI_BIT0 : (kind == 2 || kind == 3) ? URI_C
-        : kind == 5 ? URI_BIT7 : URI_ZERO;
+    rkind = (uint32_t)kind;
   }
 
   __host__ __device__ constexpr UDesc build() const {
@@ -143,9 +138,9 @@ struct UDescB {  // builder
     d.q0z = flags;
     d.q0w = keep | (comp << 8) | (set << 16) | (xr << 24);
     d.q1x = (len << UV_LEN) | (cnt << UV_CYC_NT) | (ct << UV_CYC_T) | (d8pos << UV_D8POS) | (unit << UV_UNIT) |
-            (lop << UV_LOP) | (lsel << UV_LSEL) | (rsel << UV_RSEL) | (rin << UV_RIN) | (tsel << UV_TSEL) |
-            (nw << UV_NW);
+            (lop << UV_LOP) | (lsel << UV_LSEL) | (rsel << UV_RSEL) | (tsel << UV_TSEL) | (nw << UV_NW);
     d.q1y = cmask | (cval << 8) | (d16 << UY_D16) | (vsrc << UY_VSRC) | (spd << UY_SPD);
+    d.q1z = rkind << 9;  // rotate-table row of the kind (see make_rot_table)
     return d;
   }
 };
@@ -295,6 +290,34 @@ __host__ __device__ constexpr UDesc make_udesc(int key) {
   // RST (z == 7)
   b.push_at_sp(); b.vsrc = UVS_PCN; b.tsel = UT_K; b.k16 = (uint32_t)(op & 0x38); b.cyc(16);
   return b.build();
+}
+
+// Rotate / shift / swap unit as a table (bitops.py): entry (kind << 9) |
+// (carry << 8) | x holds the result byte and the carry out (bit 8) of kind
+// RLC RRC RL RR SLA SRA SWAP SRL (0..7) applied to x with carry in `carry`
+// (SWAP's carry out is 0).
+__host__ __device__ constexpr uint32_t rot_entry(int kind, int c, int x) {
+  int r = 0, co = 0;
+  switch (kind) {
+    case 0: co = x >> 7; r = ((x << 1) & 0xFF) | co; break;
+    case 1: co = x & 1; r = (x >> 1) | (co << 7); break;
+    case 2: co = x >> 7; r = ((x << 1) & 0xFF) | c; break;
+    case 3: co = x & 1; r = (x >> 1) | (c << 7); break;
+    case 4: co = x >> 7; r = (x << 1) & 0xFF; break;
+    case 5: co = x & 1; r = (x >> 1) | (x & 0x80); break;
+    case 6: co = 0; r = ((x & 0xF) << 4) | (x >> 4); break;
+    default: co = x & 1; r = x >> 1; break;
+  }
+  return (uint32_t)r | ((uint32_t)co << 8);
+}
+constexpr int ROT_ENTRIES = 8 * 2 * 256;
+struct RotTable {
+  uint16_t v[ROT_ENTRIES];
+};
+__host__ __device__ constexpr RotTable make_rot_table() {
+  RotTable t{};
+  for (int k = 0; k < ROT_ENTRIES; k++) t.v[k] = (uint16_t)rot_entry(k >> 9, (k >> 8) & 1, k & 0xFF);
+  return t;
 }
 
 constexpr int UDESC_KEYS = 512;
