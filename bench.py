@@ -81,12 +81,12 @@ WORKLOADS = {
 # tests/test_bench_cpu.py checks these against the profile summaries. A shape
 # without a capture reports no issue roof.
 WARP_INSTR_PER_EMULATED_INSTR = {
-    "config5:uniform": (330.716229167e9 / (131072 * 193219.982), "profiles/gb_step_kernel_uniform_config5_131072envs.md"),
+    "config5:uniform": (318.771637077e9 / (131072 * 193219.982), "profiles/gb_step_kernel_uniform_config5_131072envs.md"),
     "config2:switch": (48.096002450e9 / (4096 * 197327.3), "profiles/gb_step_kernel_config2_4096envs.md"),
 }
 # dram__bytes_read.sum + dram__bytes_write.sum per env of one step-kernel
 # launch, from the same captures (None: not captured for this build).
-STEP_DRAM_BYTES_PER_ENV = {"config5:uniform": (332.23e9 + 69.46e9) / 131072, "config2:switch": None}
+STEP_DRAM_BYTES_PER_ENV = {"config5:uniform": (332.08e9 + 69.43e9) / 131072, "config2:switch": None}
 
 # Per-env state the step kernel reads at launch start and writes back at the
 # end (27 i32 + 2 i64 + 3 u8 scalars, 20 i32 cart_state words, 12 cached IO
