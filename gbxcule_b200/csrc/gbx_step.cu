@@ -1248,6 +1248,17 @@ __host__ __device__ constexpr size_t rom_smem_bytes(int P, bool uni) {
   return uni ? (((size_t)P + 16 + 15) & ~(size_t)15) : (size_t)P * 4;
 }
 __host__ __device__ constexpr size_t udesc_smem_offset(int P) { return rom_smem_bytes(P, true) + 512; }
+// Env run by lane `lane` of global warp `gw` at K envs per warp, or -1.
+// Env 0 alone takes the exact post-instruction path at every scanline (it
+// records the scanline latches), so with K > 1 it gets warp 0 to itself and
+// no other env waits on it; lane l < K of warp w >= 1 runs env 1 + (w-1)*K + l.
+__device__ __forceinline__ int lane_env(int gw, int lane, int K, int n) {
+  if (lane >= K) return -1;
+  if (K > 1 && gw == 0 && lane != 0) return -1;
+  const int env = K == 1 ? gw : gw == 0 ? 0 : 1 + (gw - 1) * K + lane;
+  return env < n ? env : -1;
+}
+
 template <int MBC, int MAXT, bool DBG, bool UNI>
 __global__ void __launch_bounds__(MAXT, 1)
     gb_step_kernel(DevState st, const uint32_t* __restrict__ pre_g, const int32_t* __restrict__ actions,
@@ -1278,15 +1289,10 @@ __global__ void __launch_bounds__(MAXT, 1)
   }
   __syncthreads();
 
-  // Env 0 alone takes the exact post-instruction path at every scanline (it
-  // records the scanline latches), so with K > 1 it gets warp 0 to itself and
-  // no other env waits on it; lane l of warp w >= 1 runs env 1 + (w-1)*K + l.
   const int lane = threadIdx.x & 31;
-  if (lane >= K) return;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (K > 1 && gw == 0 && lane != 0) return;
-  const int env = K == 1 ? gw : gw == 0 ? 0 : 1 + (gw - 1) * K + lane;
-  if (env >= st.n) return;
+  const int env = lane_env(gw, lane, K, st.n);
+  if (env < 0) return;
   const size_t S = (size_t)st.S;
 
   Emu<MBC> s;
@@ -1417,10 +1423,8 @@ __global__ void __launch_bounds__(MAXT, 1)
   if constexpr (UNI) {
     // lanes of this warp that run an env (the others returned above)
     unsigned alive = 0;
-    for (int l = 0; l < K; l++) {
-      const int e = K == 1 ? gw : gw == 0 ? (l == 0 ? 0 : st.n) : 1 + (gw - 1) * K + l;
-      if (e < st.n) alive |= 1u << l;
-    }
+    for (int l = 0; l < K; l++)
+      if (lane_env(gw, l, K, st.n) >= 0) alive |= 1u << l;
     uniform_loop<MBC>(s, h, run, ninstr, win_hi, bankN_off, cram_off, pre_s,
                       reinterpret_cast<const uint32_t*>(st.rom), pre_s_words, dec_s, ud_s, rot_s, frames_to_run,
                       alive);
