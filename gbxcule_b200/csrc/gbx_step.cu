@@ -1,5 +1,8 @@
 // gbx_step.cu - the env-step kernel: one SM83 console per thread for the whole
-// frame-skip loop.
+// frame-skip loop, with two interpreters: a switch over instruction families
+// (below) and a uniform datapath for full warps of envs at different PCs
+// (uniform_loop, gbx_udesc.h). The host picks K envs per warp and the
+// interpreter per batch by timing (gbx_api.cu).
 //
 // Semantics follow the reference kernel of bkase/gbxcule
 // (src/gbxcule/kernels/cpu_step_builder.py:876-1781 and the instruction
@@ -14,12 +17,13 @@
 //    same sector. Cached IO ports (JOYP, DIV, TIMA, TMA, TAC, IF, LCDC, STAT, LY,
 //    LYC, WY, IE) live in registers; every path that touches those addresses
 //    (CPU access, OAM DMA source, env-0 latches) goes through the cache.
-//  * Fetch: the ROM is pre-decoded on the host into one 32-bit word per byte
-//    (opcode, 16-bit immediate, family). Banks 0-1 of it sit in shared
-//    memory, so fetch + decode is a single 4-byte shared load; other banks
-//    come through the read-only path. Code outside ROM (RAM, the boot ROM
-//    overlay, bank-crossing fetches) is decoded from bytes.
-//  * Execute: one switch over 36 families of SM83's regular encoding (the
+//  * Fetch (switch): the ROM is pre-decoded on the host into one 32-bit word
+//    per byte (opcode, 16-bit immediate, family). Banks 0-1 of it sit in
+//    shared memory, so fetch + decode is a single 4-byte shared load; other
+//    banks come through the read-only path. (Uniform: raw ROM bytes, two
+//    aligned words per fetch.) Code outside ROM (RAM, the boot ROM overlay,
+//    bank-crossing fetches) is decoded from bytes.
+//  * Execute (switch): one switch over 36 families of SM83's regular encoding (the
 //    CB and ALU register forms split by operation). Registers are packed
 //    into two u32, read with one byte-permute and written with one bit-field
 //    insert; operand fields are extracted inside the cases that use them;
@@ -1801,7 +1805,7 @@ static int env_int(const char* name, int dflt) {
 }
 
 // Largest number of this kernel's warps one SM holds: one block per SM (the
-// staged ROM words fill shared memory) of at most 1024 threads.
+// staged ROM fills most of shared memory) of at most 1024 threads.
 constexpr int WARPS_PER_SM = 32;
 
 // Envs per warp that fills the GPU with one wave of warps: the smallest K in
