@@ -484,6 +484,13 @@ def run_config2(args) -> None:
                            render_pixels_packed=True, render_on_step=False, device=f"cuda:{local}")
     be.reset()
     acts_dev = torch.as_tensor(acts_host, device=dev)
+    # the launch-shape tuner's trial steps first (it times each candidate
+    # twice on the first real steps), so that no timed step runs a trial
+    tr = 0
+    while not be.envs_per_warp()[1] and tr < 16:
+        be.step_torch(acts_dev[tr % W])
+        torch.cuda.synchronize()  # the tuner reads finished trials only
+        tr += 1
     for w in range(W):
         be.step_torch(acts_dev[w])
         be.render_pixels_snapshot_torch()

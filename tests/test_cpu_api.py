@@ -57,6 +57,7 @@ def test_null_handles_are_rejected():
     assert lib.gbx_snapshot_destroy(None) == L.GBX_OK
     assert lib.gbx_set_envs_per_warp(None, 4) == L.GBX_ERR_INVALID
     assert lib.gbx_set_dispatch(None, 2) == L.GBX_ERR_INVALID
+    assert lib.gbx_render_packed_scaled(None, None, 0, None, 0, None) == L.GBX_ERR_INVALID
 
 
 def test_generators_are_deterministic_with_valid_headers():
