@@ -48,8 +48,12 @@ def _step(be, actions):
     be.step_torch(torch.as_tensor(np.asarray(actions, dtype=np.int32), device="cuda"))
 
 
+# automatic launch shape (its trial steps include the uniform interpreter),
+# and every step on the uniform interpreter at 32 envs per warp (a debug-trap
+# case keeps its trap-checking switch instantiation either way)
+@pytest.mark.parametrize("shape", ["auto", "uniform32"])
 @pytest.mark.parametrize("case", _cases(), ids=lambda c: c["name"])
-def test_golden_case_on_gpu(case, micro_roms, monkeypatch):
+def test_golden_case_on_gpu(case, shape, micro_roms, monkeypatch):
     from gbxcule_b200 import ResetCache
 
     rom = case_rom(case, micro_roms)
@@ -58,6 +62,9 @@ def test_golden_case_on_gpu(case, micro_roms, monkeypatch):
         monkeypatch.setenv(k, v)
     be = _backend(rom, n, case["frames"], case["release"], case["stage"], render_pixels=True,
                   render_pixels_packed=True, render_on_step=False, render_bg=case.get("render_bg", False))
+    if shape == "uniform32":
+        be.set_envs_per_warp(32)
+        be.set_dispatch("uniform")
     try:
         assert st.digest(be.export_state()) == case["reset_digest"]
         init = case_setup_state(case, rom)
