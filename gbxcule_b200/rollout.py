@@ -195,8 +195,11 @@ def run_rollout(backend, policy, steps: int, *, generator=None, chunk: int = 163
     # a bf16 policy reads the frames the render writes beside the packed
     # bytes (shade / 3 in bf16: the same values as unpacking and dividing),
     # in the 2x2 space-to-depth layout of its first convolution
+    # (this module's bf16 PixelPolicy; any other policy gets the unpacked
+    # uint8 frames through its forward)
     wdt = next(policy.parameters()).dtype
-    scaled = torch.empty((n, 36, 40, 4), dtype=wdt, device=dev) if wdt is torch.bfloat16 else None
+    fused = wdt is torch.bfloat16 and hasattr(policy, "forward_s2d")
+    scaled = torch.empty((n, 36, 40, 4), dtype=wdt, device=dev) if fused else None
     out = Rollout()
     with torch.no_grad():
         for k in range(steps):
